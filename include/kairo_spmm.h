@@ -1,0 +1,205 @@
+/*
+ * kairo_spmm.h -- C ABI of the B200 (sm_100a) block-sparse SpMM library.
+ *
+ * This is the drop-in boundary for Kairo's block-sparse matmul path.  It
+ * replaces the pybind11 module of the reference (csrc/bindings.cpp:84-103,
+ * 119-124) and its host wrapper acc_spmm_forward_cuda
+ * (csrc/acc_spmm_kernel.cu:158-207) with plain C entry points: raw device
+ * pointers, integer sizes, a caller-owned workspace and the caller's CUDA
+ * stream.  No C++ exception and no framework type crosses this boundary;
+ * every entry point returns a kairo_status and keeps a per-thread message
+ * that kairo_last_error_message() returns.
+ *
+ * Conventions
+ *  - All matrices are row-major.  Block (tile) storage is (nblocks, bm, bk)
+ *    row-major, the layout of the reference's A_tiles (kairo/ops/spmm.py:42-53).
+ *  - "BSR" means: row_ptr (nbr+1, int32, exclusive prefix of blocks per
+ *    block-row), col_idx (nnzb, int32, block-column of each block in row
+ *    order), and optionally blk_idx (nnzb, int32, which stored block holds
+ *    block p; NULL means block p is stored at position p).  Row order within a
+ *    block-row is the stable order of the input COO list, as produced by the
+ *    reference's _sort_coo_by_row + _coo_to_row_offsets
+ *    (kairo/ops/sparse_embedding.py:49-56, 23-46).
+ *  - Launches are asynchronous on `stream` (a cudaStream_t; NULL = legacy
+ *    default stream).  Device-side failures (an index out of range, a
+ *    pipeline wait that timed out) are recorded in the workspace error word
+ *    and read back with kairo_workspace_error().
+ *  - Workspaces are caller-allocated device memory.  They must be zero-filled
+ *    before their first use; the library leaves every counter it uses at zero
+ *    when a launch completes normally, so one workspace can be reused by
+ *    consecutive launches on one stream.  Launches that overlap in time (two
+ *    streams) must use different workspaces.
+ */
+#ifndef KAIRO_SPMM_H_
+#define KAIRO_SPMM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KAIRO_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define KAIRO_API __attribute__((visibility("default")))
+#else
+#define KAIRO_API
+#endif
+
+typedef enum kairo_status {
+  KAIRO_STATUS_SUCCESS = 0,
+  KAIRO_STATUS_INVALID_VALUE = 1,     /* bad argument (the reference raises via TORCH_CHECK) */
+  KAIRO_STATUS_NOT_SUPPORTED = 2,     /* valid input outside what the kernels implement */
+  KAIRO_STATUS_CUDA_ERROR = 3,        /* a CUDA runtime/driver call failed */
+  KAIRO_STATUS_WORKSPACE_TOO_SMALL = 4,
+  KAIRO_STATUS_DEVICE_ERROR = 5       /* the device recorded an error (see kairo_workspace_error) */
+} kairo_status;
+
+typedef enum kairo_dtype {
+  KAIRO_DTYPE_F32 = 0,
+  KAIRO_DTYPE_F16 = 1,
+  KAIRO_DTYPE_BF16 = 2
+} kairo_dtype;
+
+/* Kernel family chosen by kairo_spmm_config.kernel. */
+typedef enum kairo_kernel {
+  KAIRO_KERNEL_AUTO = 0,     /* tcgen05 for f16/bf16 when the shape allows it, else SIMT */
+  KAIRO_KERNEL_SIMT = 1,     /* CUDA-core FMA kernel (fp32 path, any shape) */
+  KAIRO_KERNEL_TCGEN05 = 2   /* TMA + tcgen05/TMEM persistent kernel (f16/bf16) */
+} kairo_kernel;
+
+/* Device error codes written to the workspace error word (low 8 bits). */
+#define KAIRO_DEVERR_NONE 0u
+#define KAIRO_DEVERR_WAIT_TIMEOUT 1u      /* a pipeline wait ran out; the kernel stopped */
+#define KAIRO_DEVERR_BAD_INDEX 2u         /* a tile row/column id outside the block grid */
+#define KAIRO_DEVERR_ROW_TOO_LONG 3u      /* unsorted COO with a block-row longer than the sort limit */
+
+/* Block-sparse matrix in BSR form (all pointers are device pointers). */
+typedef struct kairo_bsr {
+  int64_t rows;              /* M: logical rows of A */
+  int64_t cols;              /* K: logical columns of A */
+  int32_t bm;                /* block rows (tile_m) */
+  int32_t bk;                /* block columns (tile_k) */
+  int32_t nbr;               /* number of block-rows = ceil(M / bm) */
+  int32_t reserved0;
+  int64_t nnzb;              /* number of nonzero blocks */
+  int64_t nblocks_stored;    /* blocks in `blocks` storage (>= nnzb when blk_idx != NULL) */
+  const int32_t* row_ptr;    /* nbr + 1 */
+  const int32_t* col_idx;    /* nnzb */
+  const int32_t* blk_idx;    /* nnzb, or NULL for identity */
+  const void* blocks;        /* (nblocks_stored, bm, bk) row-major, dtype below */
+  kairo_dtype dtype;
+  int32_t reserved1;
+} kairo_bsr;
+
+/* Tuning knobs of one launch; zero-initialised means "library default". */
+typedef struct kairo_spmm_config {
+  int32_t kernel;            /* kairo_kernel */
+  int32_t n_tile;            /* C columns per work item on tcgen05: 128 or 256 (0 = auto) */
+  int32_t stages;            /* shared-memory pipeline depth (0 = auto) */
+  int32_t row_cost;          /* scheduler weight of one block-row in units of one block (0 = auto) */
+  int32_t num_ctas;          /* persistent grid size (0 = one CTA per SM) */
+  int32_t reserved[3];
+} kairo_spmm_config;
+
+/* Operand layouts of kairo_bsr_spmm. */
+#define KAIRO_LAYOUT_STANDARD 0  /* B is (K x N), C is (M x N):  C = A * B            */
+#define KAIRO_LAYOUT_LINEAR 1    /* X is (N x K), Y is (N x M):  Y = X * A^T (a linear layer) */
+
+/* ------------------------------------------------------------------------
+ * BSR SpMM.  STANDARD: C[M x N] = A_bsr[M x K] * B[K x N].
+ *            LINEAR:   Y[N x M] = X[N x K] * A_bsr^T, i.e. C^T with B = X^T.
+ * `b` has leading dimension ldb (elements), `c` has ldc.  B's dtype equals
+ * A->dtype; c_dtype is F32 (fp32 accumulate, fp32 out) or, in LINEAR layout,
+ * may equal A->dtype (fp32 accumulate, rounded once on store).
+ * Every element of C (all M x N) is written, including all-zero block-rows.
+ * Replaces the numerical part of acc_spmm_forward_cuda
+ * (csrc/acc_spmm_kernel.cu:158-207) for BSR input.
+ * ---------------------------------------------------------------------- */
+KAIRO_API kairo_status kairo_bsr_spmm(const kairo_bsr* a, const void* b, int64_t ldb,
+                            int32_t layout, int64_t n, void* c, int64_t ldc,
+                            kairo_dtype c_dtype, const kairo_spmm_config* cfg,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of zero-initialised workspace kairo_bsr_spmm needs for this problem. */
+KAIRO_API kairo_status kairo_bsr_spmm_workspace_size(const kairo_bsr* a, int32_t layout, int64_t n,
+                                           const kairo_spmm_config* cfg, size_t* bytes);
+
+/* ------------------------------------------------------------------------
+ * COO tile list -> BSR, on the device, bit-identical to the reference's
+ * convention: perm = argsort(tile_row_ids, stable) (sparse_embedding.py:55),
+ * col_idx = tile_col_ids[perm], row_ptr = row offsets of the sorted rows
+ * (sparse_embedding.py:23-46, here int32).  `perm` receives the stored-block
+ * index of every BSR position (use it as kairo_bsr.blk_idx).  *is_identity
+ * (host) tells whether the input was already row-sorted (perm[p] == p); when
+ * it is, callers may pass blk_idx = NULL.  Ids outside [0, nbr) x [0, nbc)
+ * raise INVALID_VALUE.  Unsorted input is supported when no block-row holds
+ * more than 16384 tiles (NOT_SUPPORTED otherwise).
+ * This call synchronises `stream` once (it reads two flags back).
+ * ---------------------------------------------------------------------- */
+KAIRO_API kairo_status kairo_bsr_build(const int32_t* tile_row_ids, const int32_t* tile_col_ids,
+                             int64_t num_tiles, int32_t nbr, int32_t nbc,
+                             int32_t* row_ptr, int32_t* col_idx, int32_t* perm,
+                             int32_t* is_identity, void* workspace, size_t workspace_bytes,
+                             void* stream);
+KAIRO_API kairo_status kairo_bsr_build_workspace_size(int64_t num_tiles, int32_t nbr, size_t* bytes);
+
+/* ------------------------------------------------------------------------
+ * Dense A (M x K, leading dimension lda) -> tiles (num_tiles, tile, tile) in
+ * COO order, zero-padding tiles that cross the right/bottom edge.  Replaces
+ * the per-tile host loop of _dense_to_block_sparse (kairo/ops/spmm.py:16-55).
+ * ---------------------------------------------------------------------- */
+KAIRO_API kairo_status kairo_dense_to_tiles(const void* a, int64_t m, int64_t k, int64_t lda,
+                                  const int32_t* tile_row_ids, const int32_t* tile_col_ids,
+                                  int64_t num_tiles, int32_t tile, kairo_dtype dtype,
+                                  void* tiles, void* stream);
+
+/* ------------------------------------------------------------------------
+ * The reference extension function acc_spmm_forward
+ * (csrc/bindings.cpp:84-103 -> csrc/acc_spmm_kernel.cu:158-207):
+ * C[M x N] (fp32, caller-allocated) = sum over tiles t of
+ * A_tiles[t] * B[col_t*tile_k : +tile_k, :] placed at rows row_t*tile_m.
+ * Tiles may come in any order (mask order); they are converted to BSR with
+ * the stable row sort above.  dtype is the dtype of A_tiles and B (the
+ * reference accepts f32 for any tile and f16 for tile 16; this library
+ * accepts f32, f16 and bf16 for tiles 16/32/64).  num_tiles == 0 writes
+ * zeros, like the reference's zero-initialised output.
+ * Synchronises `stream` once (through kairo_bsr_build).
+ * ---------------------------------------------------------------------- */
+KAIRO_API kairo_status kairo_acc_spmm_forward(const void* a_tiles, const int32_t* tile_row_ids,
+                                    const int32_t* tile_col_ids, const void* b, float* c,
+                                    int32_t m, int32_t k, int32_t n, int32_t num_tiles,
+                                    int32_t tile_m, int32_t tile_k, kairo_dtype dtype,
+                                    void* workspace, size_t workspace_bytes, void* stream);
+KAIRO_API kairo_status kairo_acc_spmm_forward_workspace_size(int32_t m, int32_t k, int32_t n,
+                                                   int32_t num_tiles, int32_t tile_m,
+                                                   int32_t tile_k, kairo_dtype dtype,
+                                                   size_t* bytes);
+
+/* ------------------------------------------------------------------------
+ * Host helper: nnz-balanced contiguous block-row partition for multi-GPU
+ * sharding.  row_ptr is a HOST array (nbr+1, int64).  bounds (parts+1) gets
+ * bounds[p] = lower_bound(row_ptr, p * nnzb / parts) (clamped, monotone),
+ * bounds[0] = 0, bounds[parts] = nbr.  The reference has no multi-GPU path;
+ * this is the partition rule of the sharded SpMM.
+ * ---------------------------------------------------------------------- */
+KAIRO_API kairo_status kairo_partition_rows(const int64_t* row_ptr, int32_t nbr, int32_t parts,
+                                  int32_t* bounds);
+
+/* Reads (and optionally clears) the device error word of a workspace.
+ * Synchronises `stream`.  *code receives KAIRO_DEVERR_* in the low 8 bits and
+ * a location tag in the upper bits (0 when no error was recorded). */
+KAIRO_API kairo_status kairo_workspace_error(void* workspace, int32_t clear, uint32_t* code,
+                                   void* stream);
+
+KAIRO_API const char* kairo_status_string(kairo_status s);
+KAIRO_API const char* kairo_last_error_message(void);
+KAIRO_API int32_t kairo_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KAIRO_SPMM_H_ */

@@ -1,0 +1,305 @@
+// Device-side COO tile list -> BSR conversion and dense -> tile gather.
+//
+// The BSR order is the reference's: a stable sort of the COO list by block
+// row (kairo/ops/sparse_embedding.py:49-56, torch.argsort(stable=True)) and
+// row offsets from per-row counts (sparse_embedding.py:23-46).  Stability is
+// obtained without a global sort: tiles are scattered into their row's bucket
+// with atomics (any order), then each bucket is sorted by original tile
+// index, which is unique, so the result equals the stable order.  Input that
+// is already row-sorted (the common case) skips both steps.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "internal.h"
+
+namespace kairo {
+namespace {
+
+constexpr int kSortMax = 16384;  // longest unsorted block-row sorted in shared memory
+constexpr int kScanThreads = 1024;
+
+// Build-workspace layout (after the 256-byte header holding the error word):
+//   flags[0] = row list not sorted, flags[1] = longest row
+struct BuildWs {
+  unsigned* err;
+  int* flags;
+  int* counts;  // [nbr]
+  int* fill;    // [nbr]
+};
+
+BuildWs carve(void* ws, int32_t nbr) {
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  BuildWs w;
+  w.err = reinterpret_cast<unsigned*>(p);
+  w.flags = reinterpret_cast<int*>(p + 64);
+  w.counts = reinterpret_cast<int*>(p + kWorkspaceHeaderBytes);
+  w.fill = w.counts + align_up(static_cast<size_t>(nbr), 64);
+  return w;
+}
+
+__global__ void k_count(const int32_t* __restrict__ rows, const int32_t* __restrict__ cols, int64_t nt, int32_t nbr,
+                        int32_t nbc, int* counts, int* flags, unsigned* err) {
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < nt;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int r = rows[t];
+    const int c = cols[t];
+    if (r < 0 || r >= nbr || c < 0 || c >= nbc) {
+      atomicCAS(err, 0u, KAIRO_DEVERR_BAD_INDEX);
+      continue;
+    }
+    atomicAdd(counts + r, 1);
+    if (t > 0 && rows[t - 1] > r) flags[0] = 1;
+  }
+}
+
+// Exclusive scan of counts into row_ptr (nbr + 1 entries) by one CTA, in
+// tiles of kScanThreads; also records the longest row.
+__global__ void __launch_bounds__(kScanThreads) k_scan(const int* __restrict__ counts, int32_t nbr,
+                                                       int32_t* __restrict__ row_ptr, int* flags) {
+  __shared__ int warp_sums[kScanThreads / 32];
+  __shared__ int carry_s;
+  if (threadIdx.x == 0) carry_s = 0;
+  int longest = 0;
+  __syncthreads();
+  for (int base = 0; base < nbr; base += kScanThreads) {
+    const int i = base + threadIdx.x;
+    const int v = i < nbr ? counts[i] : 0;
+    longest = max(longest, v);
+    int x = v;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int s = warp_sums[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, s, o);
+        if (lane >= o) s += y;
+      }
+      warp_sums[lane] = s;
+    }
+    __syncthreads();
+    const int carry = carry_s;
+    const int incl = x + (warp > 0 ? warp_sums[warp - 1] : 0) + carry;
+    if (i < nbr) row_ptr[i] = incl - v;
+    __syncthreads();
+    if (threadIdx.x == kScanThreads - 1) carry_s = incl;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) row_ptr[nbr] = carry_s;
+  // longest row
+  for (int o = 16; o > 0; o >>= 1) longest = max(longest, __shfl_xor_sync(0xffffffffu, longest, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(flags + 1, longest);
+}
+
+// Sorted input: identity permutation.  Unsorted input: scatter every tile
+// into its row bucket (order inside the bucket fixed up by k_segsort).
+__global__ void k_place(const int32_t* __restrict__ rows, const int32_t* __restrict__ cols, int64_t nt,
+                        const int32_t* __restrict__ row_ptr, int* fill, int32_t* __restrict__ col_idx,
+                        int32_t* __restrict__ perm, const int* flags, const unsigned* err) {
+  if (*err) return;
+  const bool unsorted = flags[0] != 0;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < nt;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    if (!unsorted) {
+      perm[t] = static_cast<int32_t>(t);
+      col_idx[t] = cols[t];
+    } else {
+      const int r = rows[t];
+      const int pos = row_ptr[r] + atomicAdd(fill + r, 1);
+      perm[pos] = static_cast<int32_t>(t);
+    }
+  }
+}
+
+// One CTA per block-row: bitonic sort of the row's tile indices (ascending)
+// in shared memory, then col_idx from the sorted indices.
+__global__ void __launch_bounds__(1024) k_segsort(const int32_t* __restrict__ cols, const int32_t* __restrict__ row_ptr,
+                                                  int32_t nbr, int32_t* __restrict__ col_idx,
+                                                  int32_t* __restrict__ perm, const int* flags, unsigned* err) {
+  if (flags[0] == 0 || *err) return;
+  extern __shared__ int keys[];
+  for (int r = blockIdx.x; r < nbr; r += gridDim.x) {
+    const int p0 = row_ptr[r], p1 = row_ptr[r + 1];
+    const int len = p1 - p0;
+    if (len == 0) continue;
+    if (len > kSortMax) {
+      if (threadIdx.x == 0) atomicCAS(err, 0u, KAIRO_DEVERR_ROW_TOO_LONG);
+      continue;
+    }
+    int pw = 1;
+    while (pw < len) pw <<= 1;
+    __syncthreads();
+    for (int e = threadIdx.x; e < pw; e += blockDim.x) keys[e] = e < len ? perm[p0 + e] : 0x7fffffff;
+    __syncthreads();
+    for (int k = 2; k <= pw; k <<= 1) {
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int e = threadIdx.x; e < pw; e += blockDim.x) {
+          const int l = e ^ j;
+          if (l > e) {
+            const int a = keys[e], b = keys[l];
+            const bool up = (e & k) == 0;
+            if ((a > b) == up) {
+              keys[e] = b;
+              keys[l] = a;
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    for (int e = threadIdx.x; e < len; e += blockDim.x) {
+      const int t = keys[e];
+      perm[p0 + e] = t;
+      col_idx[p0 + e] = cols[t];
+    }
+  }
+}
+
+__global__ void k_fill_zero(int* p, int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    p[i] = 0;
+}
+
+// Dense (M x K) -> tiles (num_tiles, tile, tile), zero-padded at the edges.
+// One thread copies one tile row segment of up to 8 elements.
+template <typename T>
+__global__ void k_dense_to_tiles(const T* __restrict__ a, int64_t m, int64_t k, int64_t lda,
+                                 const int32_t* __restrict__ rows, const int32_t* __restrict__ cols, int64_t nt,
+                                 int32_t tile, int32_t nbr, int32_t nbc, T* __restrict__ tiles, unsigned* err) {
+  const int segs = (tile + 7) / 8;
+  const int64_t total = nt * tile * segs;
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < total;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = g / (static_cast<int64_t>(tile) * segs);
+    const int rem = static_cast<int>(g - t * tile * segs);
+    const int rr = rem / segs;
+    const int c0 = (rem - rr * segs) * 8;
+    const int br = rows[t], bc = cols[t];
+    T* dst = tiles + (t * tile + rr) * tile;
+    const bool ok = br >= 0 && br < nbr && bc >= 0 && bc < nbc;
+    if (!ok && rr == 0 && c0 == 0 && err) atomicCAS(err, 0u, KAIRO_DEVERR_BAD_INDEX);
+    const int64_t r = static_cast<int64_t>(br) * tile + rr;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int cc = c0 + q;
+      if (cc >= tile) break;
+      const int64_t c = static_cast<int64_t>(bc) * tile + cc;
+      T v;
+      if (ok && r < m && c < k)
+        v = a[r * lda + c];
+      else
+        memset(&v, 0, sizeof(T));
+      dst[cc] = v;
+    }
+  }
+}
+
+int grid_for(int64_t work, int threads) {
+  const int64_t g = (work + threads - 1) / threads;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(g, 148 * 32)));
+}
+
+}  // namespace
+
+size_t bsr_build_ws_bytes(int64_t num_tiles, int32_t nbr) {
+  (void)num_tiles;
+  return kWorkspaceHeaderBytes + 2 * align_up(static_cast<size_t>(nbr), 64) * sizeof(int);
+}
+
+}  // namespace kairo
+
+using namespace kairo;
+
+extern "C" kairo_status kairo_bsr_build_workspace_size(int64_t num_tiles, int32_t nbr, size_t* bytes) {
+  if (!bytes || num_tiles < 0 || nbr < 0) return fail(KAIRO_STATUS_INVALID_VALUE, "invalid argument");
+  *bytes = bsr_build_ws_bytes(num_tiles, nbr);
+  return KAIRO_STATUS_SUCCESS;
+}
+
+extern "C" kairo_status kairo_bsr_build(const int32_t* tile_row_ids, const int32_t* tile_col_ids, int64_t num_tiles,
+                                        int32_t nbr, int32_t nbc, int32_t* row_ptr, int32_t* col_idx, int32_t* perm,
+                                        int32_t* is_identity, void* workspace, size_t workspace_bytes, void* stream) {
+  if (num_tiles < 0 || nbr < 0 || nbc < 0) return fail(KAIRO_STATUS_INVALID_VALUE, "negative size");
+  if (num_tiles > 0x7fffffffLL) return fail(KAIRO_STATUS_NOT_SUPPORTED, "more than 2^31-1 tiles");
+  if (!row_ptr || !workspace || (num_tiles > 0 && (!tile_row_ids || !tile_col_ids || !col_idx || !perm)))
+    return fail(KAIRO_STATUS_INVALID_VALUE, "null pointer argument");
+  if (workspace_bytes < bsr_build_ws_bytes(num_tiles, nbr))
+    return fail(KAIRO_STATUS_WORKSPACE_TOO_SMALL, "build workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  BuildWs w = carve(workspace, nbr);
+  cudaError_t e;
+  // Zero the header flags and both per-row arrays.
+  e = cudaMemsetAsync(workspace, 0, bsr_build_ws_bytes(num_tiles, nbr), s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(build workspace)");
+  if (num_tiles > 0) k_count<<<grid_for(num_tiles, 256), 256, 0, s>>>(tile_row_ids, tile_col_ids, num_tiles, nbr, nbc, w.counts, w.flags, w.err);
+  k_scan<<<1, kScanThreads, 0, s>>>(w.counts, nbr, row_ptr, w.flags);
+  if (num_tiles > 0) {
+    k_place<<<grid_for(num_tiles, 256), 256, 0, s>>>(tile_row_ids, tile_col_ids, num_tiles, row_ptr, w.fill, col_idx,
+                                                     perm, w.flags, w.err);
+    static bool attr_set[64] = {false};
+    const int dev = current_device();
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+      e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&k_segsort), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kSortMax * static_cast<int>(sizeof(int)));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_segsort)");
+      attr_set[dev] = true;
+    }
+    k_segsort<<<std::max(1, std::min(nbr, 148 * 8)), 1024, kSortMax * sizeof(int), s>>>(tile_col_ids, row_ptr, nbr,
+                                                                                       col_idx, perm, w.flags, w.err);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch of the BSR build kernels");
+  // One read-back: error word and the sorted flag.
+  unsigned hdr[32];
+  e = cudaMemcpyAsync(hdr, workspace, sizeof(hdr), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "reading the BSR build status");
+  const unsigned code = hdr[0] & 0xffu;
+  if (code == KAIRO_DEVERR_BAD_INDEX)
+    return fail(KAIRO_STATUS_INVALID_VALUE, "tile row/column id outside the block grid");
+  if (code == KAIRO_DEVERR_ROW_TOO_LONG)
+    return fail(KAIRO_STATUS_NOT_SUPPORTED, "unsorted tile list with a block-row longer than 16384 tiles");
+  if (code) return fail(KAIRO_STATUS_DEVICE_ERROR, "device error during BSR build");
+  if (is_identity) *is_identity = (reinterpret_cast<int*>(hdr)[16] == 0) ? 1 : 0;
+  return KAIRO_STATUS_SUCCESS;
+}
+
+extern "C" kairo_status kairo_dense_to_tiles(const void* a, int64_t m, int64_t k, int64_t lda,
+                                             const int32_t* tile_row_ids, const int32_t* tile_col_ids,
+                                             int64_t num_tiles, int32_t tile, kairo_dtype dtype, void* tiles,
+                                             void* stream) {
+  if (m < 0 || k < 0 || num_tiles < 0 || tile <= 0 || lda < k) return fail(KAIRO_STATUS_INVALID_VALUE, "invalid size");
+  if (num_tiles == 0) return KAIRO_STATUS_SUCCESS;
+  if (!a || !tile_row_ids || !tile_col_ids || !tiles) return fail(KAIRO_STATUS_INVALID_VALUE, "null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int32_t nbr = static_cast<int32_t>(ceil_div64(m, tile));
+  const int32_t nbc = static_cast<int32_t>(ceil_div64(k, tile));
+  const int64_t work = num_tiles * tile * ((tile + 7) / 8);
+  const int g = grid_for(work, 256);
+  switch (dtype) {
+    case KAIRO_DTYPE_F32:
+      k_dense_to_tiles<float><<<g, 256, 0, s>>>(static_cast<const float*>(a), m, k, lda, tile_row_ids, tile_col_ids,
+                                               num_tiles, tile, nbr, nbc, static_cast<float*>(tiles), nullptr);
+      break;
+    case KAIRO_DTYPE_F16:
+    case KAIRO_DTYPE_BF16:
+      k_dense_to_tiles<uint16_t><<<g, 256, 0, s>>>(static_cast<const uint16_t*>(a), m, k, lda, tile_row_ids,
+                                                  tile_col_ids, num_tiles, tile, nbr, nbc,
+                                                  static_cast<uint16_t*>(tiles), nullptr);
+      break;
+    default:
+      return fail(KAIRO_STATUS_INVALID_VALUE, "unknown dtype");
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch of the dense-to-tiles kernel");
+  return KAIRO_STATUS_SUCCESS;
+}

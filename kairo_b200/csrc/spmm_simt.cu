@@ -1,0 +1,142 @@
+// CUDA-core BSR SpMM: the fp32 path (tcgen05 kind::tf32 would lose the 1e-3
+// accuracy bar on its own) and the general path for block shapes or operand
+// alignments the tcgen05 kernel does not take.
+//
+// Same arithmetic as the reference's fp32 kernel (csrc/acc_spmm_kernel.cu:
+// 115-152) and CPU fallback (kairo/ops/spmm.py:108-134), restructured: one CTA
+// owns one block-row x 128 columns of C, walks the row's blocks in BSR order,
+// keeps the bm partial sums of its column in registers and stores C once, so
+// there are no atomics and every C element (including all-zero block-rows) is
+// written exactly once.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "internal.h"
+
+namespace kairo {
+namespace {
+
+constexpr int kSimtCols = 128;
+constexpr int kMaxBk = 64;
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+// BM_CAP: compile-time bound on bm (register array size); bm <= BM_CAP.
+template <int BM_CAP, typename TIn>
+__global__ void __launch_bounds__(kSimtCols)
+    bsr_spmm_simt_kernel(const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx,
+                         const int32_t* __restrict__ blk_idx, const TIn* __restrict__ blocks,
+                         const TIn* __restrict__ b, int64_t ldb, float* __restrict__ c, int64_t ldc, int32_t m,
+                         int64_t k, int32_t n, int32_t bm, int32_t bk, int32_t nbc, int64_t nblocks_stored,
+                         unsigned* err) {
+  // Block transposed in shared memory: As[kk][r], so one k step reads the bm
+  // values of a column as float4 broadcasts.
+  __shared__ __align__(16) float As[kMaxBk * BM_CAP];
+  const int i = blockIdx.x;
+  const int col = blockIdx.y * kSimtCols + threadIdx.x;
+  float acc[BM_CAP];
+#pragma unroll
+  for (int r = 0; r < BM_CAP; ++r) acc[r] = 0.f;
+
+  const int p_begin = row_ptr[i];
+  const int p_end = row_ptr[i + 1];
+  for (int p = p_begin; p < p_end; ++p) {
+    int cb = col_idx[p];
+    int64_t blk = blk_idx ? blk_idx[p] : p;
+    const bool bad = cb < 0 || cb >= nbc || blk < 0 || blk >= nblocks_stored;
+    if (bad) {
+      if (threadIdx.x == 0) atomicCAS(err, 0u, KAIRO_DEVERR_BAD_INDEX);
+      continue;
+    }
+    __syncthreads();
+    const TIn* src = blocks + blk * static_cast<int64_t>(bm) * bk;
+    for (int e = threadIdx.x; e < bm * bk; e += kSimtCols) {
+      const int r = e / bk, kk = e - r * bk;
+      As[kk * BM_CAP + r] = to_f32(src[e]);
+    }
+    __syncthreads();
+    if (col < n) {
+      const int64_t k0 = static_cast<int64_t>(cb) * bk;
+      for (int kk = 0; kk < bk; ++kk) {
+        const int64_t krow = k0 + kk;
+        const float bv = krow < k ? to_f32(b[krow * ldb + col]) : 0.f;
+        const float4* a4 = reinterpret_cast<const float4*>(As + kk * BM_CAP);
+#pragma unroll
+        for (int r4 = 0; r4 < BM_CAP / 4; ++r4) {
+          const float4 a = a4[r4];
+          acc[4 * r4 + 0] = fmaf(a.x, bv, acc[4 * r4 + 0]);
+          acc[4 * r4 + 1] = fmaf(a.y, bv, acc[4 * r4 + 1]);
+          acc[4 * r4 + 2] = fmaf(a.z, bv, acc[4 * r4 + 2]);
+          acc[4 * r4 + 3] = fmaf(a.w, bv, acc[4 * r4 + 3]);
+        }
+      }
+    }
+  }
+  if (col < n) {
+#pragma unroll
+    for (int r = 0; r < BM_CAP; ++r) {
+      const int64_t row = static_cast<int64_t>(i) * bm + r;
+      if (r < bm && row < m) c[row * ldc + col] = acc[r];
+    }
+  }
+}
+
+template <int BM_CAP, typename TIn>
+kairo_status launch_cap(const kairo_bsr* a, const void* b, int64_t ldb, int64_t n, void* c, int64_t ldc,
+                        void* workspace, cudaStream_t stream) {
+  // Unused rows of As (r >= bm) must read as zero: they feed acc[r] only,
+  // which is never stored, so no clearing is needed.
+  dim3 grid(static_cast<unsigned>(a->nbr), static_cast<unsigned>(ceil_div64(n, kSimtCols)));
+  bsr_spmm_simt_kernel<BM_CAP, TIn><<<grid, kSimtCols, 0, stream>>>(
+      a->row_ptr, a->col_idx, a->blk_idx, static_cast<const TIn*>(a->blocks), static_cast<const TIn*>(b), ldb,
+      static_cast<float*>(c), ldc, static_cast<int32_t>(a->rows), a->cols, static_cast<int32_t>(n), a->bm, a->bk,
+      static_cast<int32_t>(ceil_div64(a->cols, a->bk)), a->nblocks_stored, static_cast<unsigned*>(workspace));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch of the SIMT SpMM kernel");
+  return KAIRO_STATUS_SUCCESS;
+}
+
+template <typename TIn>
+kairo_status launch_typed(const kairo_bsr* a, const void* b, int64_t ldb, int64_t n, void* c, int64_t ldc,
+                          void* workspace, cudaStream_t stream) {
+  if (a->bm <= 16) return launch_cap<16, TIn>(a, b, ldb, n, c, ldc, workspace, stream);
+  if (a->bm <= 32) return launch_cap<32, TIn>(a, b, ldb, n, c, ldc, workspace, stream);
+  return launch_cap<64, TIn>(a, b, ldb, n, c, ldc, workspace, stream);
+}
+
+}  // namespace
+
+bool simt_supported(const kairo_bsr* a, int32_t layout, kairo_dtype c_dtype, std::string* why) {
+  auto no = [&](const char* w) {
+    if (why) *why = w;
+    return false;
+  };
+  if (layout != KAIRO_LAYOUT_STANDARD) return no("the SIMT kernel implements the STANDARD layout only");
+  if (c_dtype != KAIRO_DTYPE_F32) return no("the SIMT kernel writes fp32 C");
+  if (a->bm < 1 || a->bm > 64 || a->bk < 1 || a->bk > kMaxBk) return no("the SIMT kernel takes blocks up to 64x64");
+  if (a->nbr > 0x7fffffff) return no("too many block-rows");
+  return true;
+}
+
+kairo_status simt_launch(const kairo_bsr* a, const void* b, int64_t ldb, int64_t n, void* c, int64_t ldc,
+                         void* workspace, cudaStream_t stream) {
+  if (ceil_div64(n, kSimtCols) > 65535) return fail(KAIRO_STATUS_NOT_SUPPORTED, "N too large for the SIMT grid");
+  switch (a->dtype) {
+    case KAIRO_DTYPE_F32:
+      return launch_typed<float>(a, b, ldb, n, c, ldc, workspace, stream);
+    case KAIRO_DTYPE_F16:
+      return launch_typed<__half>(a, b, ldb, n, c, ldc, workspace, stream);
+    case KAIRO_DTYPE_BF16:
+      return launch_typed<__nv_bfloat16>(a, b, ldb, n, c, ldc, workspace, stream);
+  }
+  return fail(KAIRO_STATUS_INVALID_VALUE, "unknown dtype");
+}
+
+}  // namespace kairo

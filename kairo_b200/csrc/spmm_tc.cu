@@ -1,0 +1,782 @@
+// Persistent TMA + tcgen05 BSR SpMM for sm_100a.
+//
+// Math (reference: kairo/ops/spmm.py:108-134, csrc/acc_spmm_kernel.cu:33-107):
+//   C[i*bm + r, n] = sum over blocks p of block-row i, in BSR order, of
+//                    sum_k blocks[p][r][k] * B[col_idx[p]*bk + k, n]
+// accumulated in fp32.
+//
+// Formulation.  A tcgen05 MMA needs M = 128 rows, but a block has only 16-64
+// rows.  So the kernel computes the transposed product per block:
+//   C^T[n0:n0+128, rows of block] += B^T_panel[n0:n0+128, bk] * block^T
+// MMA M = 128 columns of C, MMA N = bm, MMA K = bk (bk/16 instructions).
+//   operand A = the gathered B row-panel, read MN-major straight from the
+//               row-major B (or K-major from X in the LINEAR layout);
+//   operand B = the nonzero block, K-major (row-major block storage);
+//   D in TMEM = 128 lanes (columns of C) x bm fp32 columns (rows of C).
+//
+// Roles (192 threads, one CTA per SM, persistent):
+//   warp 0      TMA producer: one A block + the matching B panel per stage;
+//   warp 1      TMEM allocator and single-thread MMA issuer;
+//   warps 2..5  epilogue: TMEM -> registers -> C, or -> a partial slot.
+// Smem stages are released by tcgen05.commit; two TMEM accumulator slots let
+// the epilogue of one block-row overlap the MMAs of the next.
+//
+// Scheduler.  Work is a merge path over (block-row heads, blocks): block-row
+// i costs `row_cost` units and each of its blocks one unit, so a chunk of 128*NT
+// columns of C is a path of W = nnzb + row_cost*nbr units.  `chunk_group`
+// consecutive chunks are concatenated and cut into gridDim.x equal ranges; all
+// CTAs therefore sweep the chunks in the same order, which keeps the B columns
+// of the current chunk resident in L2.  A block-row cut by a range boundary is
+// computed in pieces: each piece goes to a partial slot, and the CTA that
+// completes the row (an atomic arrival counter) adds the pieces in CTA order
+// and writes C.  The result is deterministic for a given grid size.
+//
+// Every mbarrier wait is bounded (ptx::wait_parity): on timeout the kernel
+// records KAIRO_DEVERR_WAIT_TIMEOUT in the workspace, drains its own copies
+// and MMAs, frees TMEM and returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <atomic>
+#include <mutex>
+#include <sstream>
+#include <unordered_map>
+
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace kairo {
+namespace {
+
+constexpr int kThreads = 192;
+constexpr uint64_t kTimeoutNs = 4000000000ull;  // 4 s of global time per wait
+constexpr int kMaxSmem = 227 * 1024;
+
+// Wait-site tags recorded with a timeout (bits 8..15 of the error word).
+enum : uint32_t { kTagEmpty = 1, kTagFull = 2, kTagTmemEmpty = 3, kTagTmemFull = 4, kTagDrain = 5 };
+
+enum RowKind : int { kSkip = 0, kZero = 1, kDirect = 2, kPartial = 3 };
+
+struct TcArgs {
+  const int32_t* row_ptr;
+  const int32_t* col_idx;
+  const int32_t* blk_idx;
+  void* c;
+  int64_t ldc;
+  int64_t w;               // path units per chunk
+  int64_t nblocks_stored;
+  unsigned* err;
+  unsigned* counters;      // this launch's bank: [ngroups][grid]
+  unsigned* counters_other;  // the other bank, zeroed by this launch
+  float* partials;         // [ngroups][grid][2][NT*BM*128]
+  int32_t m;
+  int32_t n;
+  int32_t nbr;
+  int32_t nbc;
+  int32_t chunk_group;
+  int32_t ngroups;
+  int32_t row_cost;
+  int32_t stages;
+  int32_t vec_store;       // LINEAR: rows of Y may be written with 16-byte stores
+};
+
+struct RowItem {
+  int chunk;       // global chunk index
+  int group;
+  int row;
+  int p0, p1;      // blocks of this piece
+  int kind;        // RowKind
+  int slot;        // partial slot this CTA writes (0 head, 1 tail)
+  int b_lo, b_hi;  // contributing CTAs of a split row
+  int lo_slot;     // slot used by b_lo
+};
+
+// Largest i in [0, nbr) with row_ptr[i] + R*i <= target, found by the whole
+// CTA with a (blockDim)-ary search; every thread returns the same value.
+__device__ int cta_find_row(const int32_t* __restrict__ row_ptr, int nbr, int R, int64_t target) {
+  int lo = 0, hi = nbr;
+  const int T = blockDim.x;
+  while (hi - lo > 1) {
+    const int span = hi - lo;
+    const int np = min(T, span - 1);
+    const int t = threadIdx.x;
+    bool pred = false;
+    if (t < np) {
+      const int idx = lo + 1 + static_cast<int>(static_cast<int64_t>(t) * (span - 1) / np);
+      pred = static_cast<int64_t>(__ldg(row_ptr + idx)) + static_cast<int64_t>(R) * idx <= target;
+    }
+    const int cnt = __syncthreads_count(pred);
+    const int nlo = cnt > 0 ? lo + 1 + static_cast<int>(static_cast<int64_t>(cnt - 1) * (span - 1) / np) : lo;
+    const int nhi = cnt < np ? lo + 1 + static_cast<int>(static_cast<int64_t>(cnt) * (span - 1) / np) : hi;
+    lo = nlo;
+    hi = nhi;
+  }
+  return lo;
+}
+
+// Walks this CTA's share of the work in launch order and calls f(item) for
+// every (chunk, block-row) piece it touches.  Warp-uniform: all 32 lanes call
+// f with the same item.  Returns false as soon as f returns false.
+template <class F>
+__device__ __forceinline__ bool walk_items(const TcArgs& a, int64_t s, int64_t e, int i_start,
+                                           int lane, F&& f) {
+  const int G = gridDim.x;
+  const int b = blockIdx.x;
+  const int64_t W = a.w;
+  const int64_t R = a.row_cost;
+  const int64_t L = W * a.chunk_group;
+  const int32_t* __restrict__ row_ptr = a.row_ptr;
+  const int64_t j_first = s / W;
+  const int64_t j_last = (e - 1) / W;
+  for (int g = 0; g < a.ngroups; ++g) {
+    for (int64_t jl = j_first; jl <= j_last; ++jl) {
+      const int64_t ls = max(s, jl * W) - jl * W;
+      const int64_t le = min(e, (jl + 1) * W) - jl * W;
+      int i = (jl == j_first) ? i_start : 0;
+      int base = -64, v = 0, v32 = 0;
+      while (i < a.nbr) {
+        if (i - base >= 32) {
+          base = i;
+          v = __ldg(row_ptr + min(base + lane, a.nbr));
+          v32 = __ldg(row_ptr + min(base + 32, a.nbr));
+        }
+        const int k = i - base;
+        const int r0 = __shfl_sync(0xffffffffu, v, k);
+        const int r1n = __shfl_sync(0xffffffffu, v, min(k + 1, 31));
+        const int r1 = (k == 31) ? v32 : r1n;
+        const int64_t P = static_cast<int64_t>(r0) + R * i;
+        if (P >= le) break;
+        RowItem it;
+        it.chunk = g * a.chunk_group + static_cast<int>(jl);
+        it.group = g;
+        it.row = i;
+        it.slot = 0;
+        it.b_lo = it.b_hi = b;
+        it.lo_slot = 0;
+        const int64_t shift = R * (i + 1);  // block p sits at path position p + shift
+        if (r1 == r0) {
+          it.kind = (P >= ls) ? kZero : kSkip;
+          it.p0 = it.p1 = r0;
+        } else {
+          const int64_t q0 = max(static_cast<int64_t>(r0), ls - shift);
+          const int64_t q1 = min(static_cast<int64_t>(r1), le - shift);
+          it.p0 = static_cast<int>(q0);
+          it.p1 = static_cast<int>(q1);
+          if (q0 >= q1) {
+            it.kind = kSkip;
+          } else if (q0 == r0 && q1 == r1) {
+            it.kind = kDirect;
+          } else {
+            it.kind = kPartial;
+            it.slot = (jl == j_first && i == i_start) ? 0 : 1;
+            const int64_t off = jl * W;
+            const int64_t d_first = off + r0 + shift;
+            const int64_t d_last = off + r1 - 1 + shift;
+            it.b_lo = static_cast<int>(((d_first + 1) * G - 1) / L);
+            it.b_hi = static_cast<int>(((d_last + 1) * G - 1) / L);
+            const int64_t s_lo = static_cast<int64_t>(it.b_lo) * L / G;
+            it.lo_slot = (s_lo >= off + P) ? 0 : 1;
+          }
+        }
+        if (it.kind != kSkip) {
+          if (!f(it)) return false;
+        }
+        ++i;
+      }
+    }
+  }
+  return true;
+}
+
+template <typename TOut>
+__device__ __forceinline__ void store_scalar(TOut* p, float v);
+template <>
+__device__ __forceinline__ void store_scalar<float>(float* p, float v) { __stcs(p, v); }
+template <>
+__device__ __forceinline__ void store_scalar<__nv_bfloat16>(__nv_bfloat16* p, float v) {
+  *p = __float2bfloat16_rn(v);
+}
+template <>
+__device__ __forceinline__ void store_scalar<__half>(__half* p, float v) { *p = __float2half_rn(v); }
+
+// Writes 16 accumulator values of one thread: rows/cols as described in the
+// file header.  `col` is this thread's column of C (STANDARD) or row of Y
+// (LINEAR); rows j0..j0+15 of block-row i.
+template <bool LINEAR, typename TOut>
+__device__ __forceinline__ void store16(const TcArgs& a, int i, int bm, int j0, int col,
+                                        const float* v) {
+  if (col >= a.n) return;
+  const int row0 = i * bm + j0;
+  if (!LINEAR) {
+    float* c = static_cast<float*>(a.c);
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj) {
+      const int r = row0 + jj;
+      if (r < a.m) __stcs(c + static_cast<int64_t>(r) * a.ldc + col, v[jj]);
+    }
+  } else {
+    TOut* y = static_cast<TOut*>(a.c) + static_cast<int64_t>(col) * a.ldc + row0;
+    if (a.vec_store && row0 + 16 <= a.m) {
+      if constexpr (sizeof(TOut) == 4) {
+        float4* y4 = reinterpret_cast<float4*>(y);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) y4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      } else {
+        uint32_t w[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          TOut lo, hi;
+          store_scalar<TOut>(&lo, v[2 * q]);
+          store_scalar<TOut>(&hi, v[2 * q + 1]);
+          w[q] = static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&lo)) |
+                 (static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+        }
+        uint4* y4 = reinterpret_cast<uint4*>(y);
+        y4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        y4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      }
+    } else {
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj)
+        if (row0 + jj < a.m) store_scalar<TOut>(y + jj, v[jj]);
+    }
+  }
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// OR of `pred` over the 128 epilogue threads (named barrier 1).  Used so that
+// the four epilogue warps always leave the work loop at the same item; a warp
+// that left alone would strand the others at the next named barrier.
+__device__ __forceinline__ bool epi_any(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t"
+      ".reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t"
+      "}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred))
+      : "memory");
+  return r != 0;
+}
+
+template <int BM, int BK, int NT, bool LINEAR, int IN_FMT, typename TOut>
+__global__ void __launch_bounds__(kThreads, 1)
+    bsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                       const __grid_constant__ CUtensorMap tmap_b, const TcArgs args) {
+  constexpr int PANEL_BYTES = NT * 128 * BK * 2;
+  constexpr int A_BYTES = BM * BK * 2;
+  constexpr int A_BYTES_PAD = (A_BYTES + 1023) / 1024 * 1024;
+  constexpr int STAGE_BYTES = PANEL_BYTES + A_BYTES_PAD;
+  constexpr uint32_t TX_BYTES = PANEL_BYTES + A_BYTES;
+  constexpr int ACC_COLS = NT * BM;
+  constexpr uint32_t TMEM_COLS = (2 * ACC_COLS <= 32) ? 32 : (2 * ACC_COLS <= 64) ? 64
+                                 : (2 * ACC_COLS <= 128) ? 128 : (2 * ACC_COLS <= 256) ? 256 : 512;
+  constexpr uint32_t IDESC = ptx::make_idesc_f16(IN_FMT, LINEAR ? 0u : 1u, 0u, 128u, BM);
+  constexpr uint32_t SW_ROW = ptx::swizzle_code_for_row_bytes(BK * 2);
+  constexpr int PART_ELEMS = NT * BM * 128;
+  static_assert(BK % 16 == 0 && BM % 16 == 0 && BM <= 256, "block shape");
+  static_assert(2 * ACC_COLS <= 512, "TMEM budget");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int S = args.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * STAGE_BYTES);
+  uint64_t* empty = full + S;
+  uint64_t* tfull = empty + S;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  int* misc = reinterpret_cast<int*>(mma_done + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 0);
+  volatile int* abort_flag = misc + 1;
+  int* red_flag = misc + 3;
+  int* issued = misc + 4;  // [S]: parity+1 of the last load issued into each stage
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      ptx::mbar_init(&full[s], 1);
+      ptx::mbar_init(&empty[s], 1);
+      issued[s] = 0;
+    }
+    for (int k = 0; k < 2; ++k) {
+      ptx::mbar_init(&tfull[k], 1);
+      ptx::mbar_init(&tempty[k], 4);
+    }
+    ptx::mbar_init(mma_done, 1);
+    misc[1] = 0;
+    misc[2] = 0;
+    ptx::mbar_init_fence();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tmap(&tmap_a);
+    ptx::prefetch_tmap(&tmap_b);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(tmem_slot, TMEM_COLS);
+    ptx::tmem_relinquish();
+  }
+
+  // Clear the counter bank the next launch on this workspace will use.
+  for (int i = blockIdx.x * kThreads + threadIdx.x; i < kCounterBankEntries; i += gridDim.x * kThreads)
+    args.counters_other[i] = 0u;
+
+  const int G = gridDim.x;
+  const int64_t L = args.w * args.chunk_group;
+  const int64_t s_range = static_cast<int64_t>(blockIdx.x) * L / G;
+  const int64_t e_range = static_cast<int64_t>(blockIdx.x + 1) * L / G;
+  const int64_t ls0 = s_range - (s_range / args.w) * args.w;
+  const int i_start = cta_find_row(args.row_ptr, args.nbr, args.row_cost, ls0);
+
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    const uint64_t pol_a = ptx::policy_evict_first();
+    const uint64_t pol_b = ptx::policy_evict_last();
+    int stage = 0;
+    uint32_t phase = 0;
+    walk_items(args, s_range, e_range, i_start, lane, [&](const RowItem& it) -> bool {
+      if (it.kind != kDirect && it.kind != kPartial) return true;
+      const int n0 = it.chunk * NT * 128;
+      for (int pb = it.p0; pb < it.p1; pb += 32) {
+        const int cnt = min(32, it.p1 - pb);
+        int mc = 0, mb = 0;
+        if (lane < cnt) {
+          mc = __ldg(args.col_idx + pb + lane);
+          mb = args.blk_idx ? __ldg(args.blk_idx + pb + lane) : pb + lane;
+          if (static_cast<unsigned>(mc) >= static_cast<unsigned>(args.nbc) ||
+              mb < 0 || static_cast<int64_t>(mb) >= args.nblocks_stored) {
+            atomicCAS(args.err, 0u, KAIRO_DEVERR_BAD_INDEX);
+            mc = 0;
+            mb = 0;
+          }
+        }
+        for (int q = 0; q < cnt; ++q) {
+          const int c = __shfl_sync(0xffffffffu, mc, q);
+          const int blk = __shfl_sync(0xffffffffu, mb, q);
+          int ok = 1;
+          if (lane == 0) {
+            ok = ptx::wait_parity(&empty[stage], phase ^ 1u, abort_flag, args.err, kTagEmpty, kTimeoutNs);
+            if (ok) {
+              uint8_t* st = smem + stage * STAGE_BYTES;
+              ptx::mbar_arrive_expect_tx(&full[stage], TX_BYTES);
+              ptx::tma_load_2d(st + PANEL_BYTES, &tmap_a, 0, blk * BM, &full[stage], pol_a);
+              if (!LINEAR) {
+#pragma unroll
+                for (int h = 0; h < 2 * NT; ++h)
+                  ptx::tma_load_2d(st + h * BK * 128, &tmap_b, n0 + 64 * h, c * BK, &full[stage], pol_b);
+              } else {
+#pragma unroll
+                for (int t = 0; t < NT; ++t)
+                  ptx::tma_load_2d(st + t * 128 * BK * 2, &tmap_b, c * BK, n0 + 128 * t, &full[stage], pol_b);
+              }
+              issued[stage] = static_cast<int>(phase) + 1;
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) return false;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      return true;
+    });
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    int slot = 0;
+    uint32_t aphase = 0;
+    walk_items(args, s_range, e_range, i_start, lane, [&](const RowItem& it) -> bool {
+      if (it.kind != kDirect && it.kind != kPartial) return true;
+      int ok = 1;
+      if (lane == 0)
+        ok = ptx::wait_parity(&tempty[slot], aphase ^ 1u, abort_flag, args.err, kTagTmemEmpty, kTimeoutNs);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) return false;
+      ptx::tc_fence_after();
+      const uint32_t d_base = tmem_base + static_cast<uint32_t>(slot * ACC_COLS);
+      for (int p = it.p0; p < it.p1; ++p) {
+        if (lane == 0) {
+          ok = ptx::wait_parity(&full[stage], phase, abort_flag, args.err, kTagFull, kTimeoutNs);
+          if (ok) {
+            ptx::tc_fence_after();
+            const uint32_t st = ptx::smem_u32(smem + stage * STAGE_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              const uint64_t bdesc = ptx::make_smem_desc(st + PANEL_BYTES + kk * 32, 16, 8 * BK * 2, SW_ROW);
+#pragma unroll
+              for (int t = 0; t < NT; ++t) {
+                uint64_t adesc;
+                if (!LINEAR)
+                  adesc = ptx::make_smem_desc(st + t * 2 * BK * 128 + kk * 2048, BK * 128, 1024, 2u);
+                else
+                  adesc = ptx::make_smem_desc(st + t * 128 * BK * 2 + kk * 32, 16, 8 * BK * 2, SW_ROW);
+                ptx::mma_f16_ss(d_base + t * BM, adesc, bdesc, IDESC, (p > it.p0 || kk > 0) ? 1u : 0u);
+              }
+            }
+            ptx::mma_commit(&empty[stage]);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) return false;
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (lane == 0) ptx::mma_commit(&tfull[slot]);
+      __syncwarp();
+      slot ^= 1;
+      if (slot == 0) aphase ^= 1u;
+      return true;
+    });
+    // Every MMA issued above has completed once mma_done flips.
+    if (lane == 0) {
+      ptx::mma_commit(mma_done);
+      int dummy = 0;
+      ptx::wait_parity(mma_done, 0, reinterpret_cast<volatile int*>(&dummy), args.err, kTagDrain, kTimeoutNs);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;          // TMEM lane quarter this warp may access
+    const int e = q * 32 + lane;     // TMEM lane == column within a 128-wide sub-tile
+    const uint32_t lane_addr = static_cast<uint32_t>(q * 32) << 16;
+    int slot = 0;
+    uint32_t aphase = 0;
+    walk_items(args, s_range, e_range, i_start, lane, [&](const RowItem& it) -> bool {
+      const int n0 = it.chunk * NT * 128;
+      if (it.kind == kZero) {
+        float z[16];
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) z[jj] = 0.f;
+#pragma unroll
+        for (int t = 0; t < NT; ++t)
+#pragma unroll
+          for (int j0 = 0; j0 < BM; j0 += 16) store16<LINEAR, TOut>(args, it.row, BM, j0, n0 + t * 128 + e, z);
+        return true;
+      }
+      int ok = 1;
+      if (lane == 0)
+        ok = ptx::wait_parity(&tfull[slot], aphase, abort_flag, args.err, kTagTmemFull, kTimeoutNs);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (epi_any(!ok)) return false;
+      ptx::tc_fence_after();
+      float* part = nullptr;
+      if (it.kind == kPartial)
+        part = args.partials + (static_cast<int64_t>(it.group * G + blockIdx.x) * 2 + it.slot) * PART_ELEMS;
+#pragma unroll
+      for (int t = 0; t < NT; ++t) {
+#pragma unroll
+        for (int j0 = 0; j0 < BM; j0 += 16) {
+          float v[16];
+          ptx::tmem_ld16(tmem_base + lane_addr + static_cast<uint32_t>(slot * ACC_COLS + t * BM + j0), v);
+          ptx::tmem_wait_ld();
+          if (it.kind == kDirect) {
+            store16<LINEAR, TOut>(args, it.row, BM, j0, n0 + t * 128 + e, v);
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) part[(t * BM + j0 + jj) * 128 + e] = v[jj];
+          }
+        }
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&tempty[slot]);
+      slot ^= 1;
+      if (slot == 0) aphase ^= 1u;
+      if (it.kind == kPartial) {
+        __threadfence();
+        epi_bar();
+        if (threadIdx.x == 64) {
+          const unsigned old = atomicAdd(args.counters + it.group * G + it.b_lo, 1u);
+          *red_flag = (old == static_cast<unsigned>(it.b_hi - it.b_lo)) ? 1 : 0;
+        }
+        epi_bar();
+        if (*red_flag) {
+          __threadfence();
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+#pragma unroll
+            for (int j0 = 0; j0 < BM; j0 += 16) {
+              float acc[16];
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) acc[jj] = 0.f;
+              for (int bb = it.b_lo; bb <= it.b_hi; ++bb) {
+                const int sl = (bb == it.b_lo) ? it.lo_slot : 0;
+                const float* src = args.partials + (static_cast<int64_t>(it.group * G + bb) * 2 + sl) * PART_ELEMS;
+#pragma unroll
+                for (int jj = 0; jj < 16; ++jj) acc[jj] += __ldcg(src + (t * BM + j0 + jj) * 128 + e);
+              }
+              store16<LINEAR, TOut>(args, it.row, BM, j0, n0 + t * 128 + e, acc);
+            }
+          }
+          if (threadIdx.x == 64) atomicExch(args.counters + it.group * G + it.b_lo, 0u);
+        }
+      }
+      return true;
+    });
+  }
+
+  __syncthreads();
+  if (warp == 0 && lane == 0 && *abort_flag) {
+    // A wait gave up: let the loads this CTA issued land before it exits.
+    int dummy = 0;
+    for (int s = 0; s < S; ++s)
+      if (issued[s])
+        ptx::wait_parity(&full[s], static_cast<uint32_t>(issued[s] - 1), reinterpret_cast<volatile int*>(&dummy),
+                         args.err, kTagDrain, kTimeoutNs);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+CUtensorMapSwizzle swizzle_for_bytes(int inner_bytes) {
+  return inner_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+         : inner_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                             : CU_TENSOR_MAP_SWIZZLE_32B;
+}
+
+kairo_status make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
+                         uint64_t inner, uint64_t outer, uint64_t row_stride_elems, uint32_t box_inner,
+                         uint32_t box_outer, const char* what) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(KAIRO_STATUS_CUDA_ERROR, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_stride_elems * static_cast<uint64_t>(elem_bytes)};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle_for_bytes(static_cast<int>(box_inner) * elem_bytes), CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    std::ostringstream os;
+    os << "cuTensorMapEncodeTiled failed for " << what << " (CUresult " << static_cast<int>(r) << ")";
+    return fail(KAIRO_STATUS_INVALID_VALUE, os.str());
+  }
+  return KAIRO_STATUS_SUCCESS;
+}
+
+constexpr int stage_bytes(int bm, int bk, int nt) {
+  return nt * 128 * bk * 2 + (bm * bk * 2 + 1023) / 1024 * 1024;
+}
+
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, TcArgs);
+
+template <int BM, int NT, bool LINEAR, int IN_FMT, typename TOut>
+KernelFn pick4() {
+  return reinterpret_cast<KernelFn>(&bsr_spmm_tc_kernel<BM, BM, NT, LINEAR, IN_FMT, TOut>);
+}
+
+template <bool LINEAR, int IN_FMT, typename TOut>
+KernelFn pick3(int bm, int nt) {
+#define KAIRO_TC_CASE(B, T) \
+  if (bm == B && nt == T) return pick4<B, T, LINEAR, IN_FMT, TOut>();
+  KAIRO_TC_CASE(16, 1)
+  KAIRO_TC_CASE(16, 2)
+  KAIRO_TC_CASE(32, 1)
+  KAIRO_TC_CASE(32, 2)
+  KAIRO_TC_CASE(64, 1)
+  KAIRO_TC_CASE(64, 2)
+#undef KAIRO_TC_CASE
+  return nullptr;
+}
+
+KernelFn pick_kernel(int bm, int nt, bool linear, kairo_dtype in, kairo_dtype out) {
+  if (!linear) {
+    if (out != KAIRO_DTYPE_F32) return nullptr;
+    return in == KAIRO_DTYPE_F16 ? pick3<false, 0, float>(bm, nt) : pick3<false, 1, float>(bm, nt);
+  }
+  if (in == KAIRO_DTYPE_F16) {
+    if (out == KAIRO_DTYPE_F32) return pick3<true, 0, float>(bm, nt);
+    if (out == KAIRO_DTYPE_F16) return pick3<true, 0, __half>(bm, nt);
+  } else {
+    if (out == KAIRO_DTYPE_F32) return pick3<true, 1, float>(bm, nt);
+    if (out == KAIRO_DTYPE_BF16) return pick3<true, 1, __nv_bfloat16>(bm, nt);
+  }
+  return nullptr;
+}
+
+size_t elem_size(kairo_dtype d) { return d == KAIRO_DTYPE_F32 ? 4 : 2; }
+
+// Counter bank of the next launch on `workspace` (alternates per workspace).
+int next_counter_bank(void* workspace) {
+  static std::mutex mu;
+  static std::unordered_map<void*, int> parity;
+  std::lock_guard<std::mutex> lock(mu);
+  int& b = parity[workspace];
+  const int use = b;
+  b ^= 1;
+  return use;
+}
+
+}  // namespace
+
+bool tc_supported(const kairo_bsr* a, int32_t layout, int64_t n, int64_t ldb, int64_t ldc, kairo_dtype c_dtype,
+                  const void* b, const void* c, std::string* why) {
+  auto no = [&](const char* w) {
+    if (why) *why = w;
+    return false;
+  };
+  if (a->dtype != KAIRO_DTYPE_F16 && a->dtype != KAIRO_DTYPE_BF16) return no("tcgen05 path needs f16 or bf16 input");
+  if (a->bm != a->bk) return no("tcgen05 path needs square blocks");
+  if (a->bm != 16 && a->bm != 32 && a->bm != 64) return no("tcgen05 path supports blocks of 16, 32 or 64");
+  if (ldb % 8 != 0) return no("B leading dimension must be a multiple of 8 elements (16-byte TMA stride)");
+  if ((reinterpret_cast<uintptr_t>(b) & 15u) || (reinterpret_cast<uintptr_t>(a->blocks) & 15u))
+    return no("B and block storage must be 16-byte aligned");
+  if (a->nblocks_stored * a->bm > INT32_MAX || a->cols > INT32_MAX || n > INT32_MAX || a->rows > INT32_MAX)
+    return no("problem exceeds 32-bit TMA coordinates");
+  if (layout == KAIRO_LAYOUT_STANDARD) {
+    if (c_dtype != KAIRO_DTYPE_F32) return no("STANDARD layout writes fp32 C");
+  } else {
+    if (c_dtype != KAIRO_DTYPE_F32 && c_dtype != a->dtype) return no("LINEAR output must be fp32 or the input dtype");
+  }
+  (void)ldc;
+  (void)c;
+  return true;
+}
+
+kairo_status tc_plan(const kairo_bsr* a, int32_t layout, int64_t n, const kairo_spmm_config* cfg, int device,
+                     TcPlan* plan) {
+  TcPlan p{};
+  p.bm = a->bm;
+  p.bk = a->bk;
+  int nt = 1;
+  if (cfg && cfg->n_tile) {
+    if (cfg->n_tile != 128 && cfg->n_tile != 256) return fail(KAIRO_STATUS_INVALID_VALUE, "n_tile must be 128 or 256");
+    nt = cfg->n_tile / 128;
+  } else {
+    // Two sub-tiles halve block re-reads when the B operand stays in L2;
+    // a single 128-column chunk keeps the L2-resident slice of a large B small.
+    const double b_bytes = static_cast<double>(a->cols) * static_cast<double>(n) * 2.0;
+    nt = (n > 128 && (layout == KAIRO_LAYOUT_LINEAR || b_bytes <= 64.0 * 1024 * 1024)) ? 2 : 1;
+  }
+  p.nt = nt;
+  p.nchunks = static_cast<int>(ceil_div64(n, 128 * nt));
+  p.row_cost = (cfg && cfg->row_cost > 0) ? cfg->row_cost : 2;
+  p.w = a->nnzb + static_cast<int64_t>(p.row_cost) * a->nbr;
+  const int sms = device_sm_count(device);
+  int grid = (cfg && cfg->num_ctas > 0) ? cfg->num_ctas : sms;
+  if (grid > kCounterBankEntries) grid = kCounterBankEntries;
+  // Smallest chunk group (a divisor of nchunks) whose counters fit one bank.
+  p.chunk_group = p.nchunks;
+  for (int cg = 1; cg <= p.nchunks; ++cg) {
+    if (p.nchunks % cg) continue;
+    if (static_cast<int64_t>(p.nchunks / cg) * grid <= kCounterBankEntries) {
+      p.chunk_group = cg;
+      break;
+    }
+  }
+  p.ngroups = p.nchunks / p.chunk_group;
+  const int64_t L = p.w * p.chunk_group;
+  if (grid > L) grid = static_cast<int>(L);
+  if (grid < 1) grid = 1;
+  p.grid = grid;
+  const int sb = stage_bytes(p.bm, p.bk, nt);
+  const int reserve = 1024 /*alignment*/ + 1024 /*barriers and flags*/;
+  int max_stages = (kMaxSmem - reserve) / sb;
+  if (max_stages > 16) max_stages = 16;
+  int stages = (cfg && cfg->stages > 0) ? std::min(cfg->stages, max_stages) : max_stages;
+  if (stages < 2) return fail(KAIRO_STATUS_NOT_SUPPORTED, "shared memory too small for two pipeline stages");
+  p.stages = stages;
+  p.smem_bytes = static_cast<size_t>(stages) * sb + reserve;
+  p.counters_offset = kWorkspaceHeaderBytes;
+  p.counters_bytes = kCounterRegionBytes;
+  p.partials_offset = p.counters_offset + p.counters_bytes;
+  p.partials_bytes = static_cast<size_t>(p.ngroups) * grid * 2 * nt * p.bm * 128 * sizeof(float);
+  p.workspace_bytes = p.partials_offset + p.partials_bytes;
+  *plan = p;
+  return KAIRO_STATUS_SUCCESS;
+}
+
+kairo_status tc_launch(const kairo_bsr* a, const void* b, int64_t ldb, int32_t layout, int64_t n, void* c,
+                       int64_t ldc, kairo_dtype c_dtype, const TcPlan& plan, void* workspace, cudaStream_t stream) {
+  const bool linear = layout == KAIRO_LAYOUT_LINEAR;
+  KernelFn fn = pick_kernel(plan.bm, plan.nt, linear, a->dtype, c_dtype);
+  if (!fn) return fail(KAIRO_STATUS_NOT_SUPPORTED, "no tcgen05 kernel for this block size / dtype combination");
+  const CUtensorMapDataType dt =
+      a->dtype == KAIRO_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap map_a, map_b;
+  kairo_status st = make_map_2d(&map_a, a->blocks, dt, 2, static_cast<uint64_t>(a->bk),
+                                static_cast<uint64_t>(a->nblocks_stored) * a->bm, static_cast<uint64_t>(a->bk),
+                                static_cast<uint32_t>(a->bk), static_cast<uint32_t>(a->bm), "block storage");
+  if (st) return st;
+  if (!linear)
+    st = make_map_2d(&map_b, b, dt, 2, static_cast<uint64_t>(n), static_cast<uint64_t>(a->cols),
+                     static_cast<uint64_t>(ldb), 64, static_cast<uint32_t>(a->bk), "B");
+  else
+    st = make_map_2d(&map_b, b, dt, 2, static_cast<uint64_t>(a->cols), static_cast<uint64_t>(n),
+                     static_cast<uint64_t>(ldb), static_cast<uint32_t>(a->bk), 128, "X");
+  if (st) return st;
+
+  TcArgs args{};
+  args.row_ptr = a->row_ptr;
+  args.col_idx = a->col_idx;
+  args.blk_idx = a->blk_idx;
+  args.c = c;
+  args.ldc = ldc;
+  args.w = plan.w;
+  args.nblocks_stored = a->nblocks_stored;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  args.err = reinterpret_cast<unsigned*>(ws);
+  const int bank = next_counter_bank(workspace);
+  unsigned* banks = reinterpret_cast<unsigned*>(ws + plan.counters_offset);
+  args.counters = banks + bank * kCounterBankEntries;
+  args.counters_other = banks + (1 - bank) * kCounterBankEntries;
+  args.partials = reinterpret_cast<float*>(ws + plan.partials_offset);
+  args.m = static_cast<int32_t>(a->rows);
+  args.n = static_cast<int32_t>(n);
+  args.nbr = a->nbr;
+  args.nbc = static_cast<int32_t>(ceil_div64(a->cols, a->bk));
+  args.chunk_group = plan.chunk_group;
+  args.ngroups = plan.ngroups;
+  args.row_cost = plan.row_cost;
+  args.stages = plan.stages;
+  const size_t osz = elem_size(c_dtype);
+  args.vec_store = linear && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0) && ((ldc * osz) % 16 == 0) ? 1 : 0;
+
+  cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(plan.smem_bytes));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+  fn<<<plan.grid, kThreads, plan.smem_bytes, stream>>>(map_a, map_b, args);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch of the tcgen05 SpMM kernel");
+  return KAIRO_STATUS_SUCCESS;
+}
+
+}  // namespace kairo

@@ -1,0 +1,41 @@
+"""kairo_b200.ops: the block-sparse SpMM operators (CUDA only).
+
+Mirrors the SpMM part of the reference's ``kairo.ops`` export surface
+(kairo/ops/__init__.py:5-17): ``block_sparse_mm`` and ``cuda_ext_available``,
+plus the BSR-level operators of this package.
+"""
+
+from __future__ import annotations
+
+from kairo_b200.ops._autotuner import TileAutotuner, TileConfig
+from kairo_b200.ops.spmm import (
+    KernelConfig,
+    block_sparse_mm,
+    block_sparse_mm_bsr,
+    bsr_from_mask,
+    bsr_from_tiles,
+    sparse_linear,
+)
+
+
+def cuda_ext_available() -> bool:
+    """True if the native library (libkairo_spmm.so) is built and loadable.
+
+    Same role as the reference's check of ``kairo._C``
+    (kairo/ops/sparse_embedding.py:14-20)."""
+    from kairo_b200 import _lib
+
+    return _lib.available()
+
+
+__all__ = [
+    "cuda_ext_available",
+    "block_sparse_mm",
+    "block_sparse_mm_bsr",
+    "bsr_from_mask",
+    "bsr_from_tiles",
+    "sparse_linear",
+    "KernelConfig",
+    "TileAutotuner",
+    "TileConfig",
+]

@@ -1,0 +1,276 @@
+"""Block-sparse matrix multiplication on B200: operators over the C ABI.
+
+``block_sparse_mm`` keeps the reference operator's signature, argument
+checks and results (kairo/ops/spmm.py:58-105) and runs only on CUDA tensors:
+the dense A is tiled by a device gather (replacing the per-tile host loop of
+spmm.py:48-53), the tiles go through ``_C.acc_spmm_forward`` and the result is
+fp32, as on the reference's CUDA path (csrc/acc_spmm_kernel.cu:169-170).
+
+The BSR-level operators (``block_sparse_mm_bsr``, ``sparse_linear``) take a
+:class:`~kairo_b200.types.BlockSparseMatrix` directly, for matrices whose
+dense form does not fit in memory.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+from torch import Tensor
+
+from kairo_b200 import _C, _lib
+from kairo_b200.types import BlockSparseMatrix, SparseMask
+
+
+@dataclass(frozen=True)
+class KernelConfig:
+    """Launch knobs of the BSR SpMM (0 = library default).
+
+    kernel: "auto", "simt" or "tcgen05"; n_tile: C columns per work item on
+    the tcgen05 kernel (128 or 256); stages: shared-memory pipeline depth;
+    row_cost: scheduler weight of a block-row in units of one block;
+    num_ctas: persistent grid size.
+    """
+
+    kernel: str = "auto"
+    n_tile: int = 0
+    stages: int = 0
+    row_cost: int = 0
+    num_ctas: int = 0
+
+    def __post_init__(self) -> None:
+        if self.kernel not in ("auto", "simt", "tcgen05"):
+            raise ValueError(f"kernel must be 'auto', 'simt' or 'tcgen05', got {self.kernel!r}")
+        if self.n_tile not in (0, 128, 256):
+            raise ValueError(f"n_tile must be 0, 128 or 256, got {self.n_tile}")
+        for name in ("stages", "row_cost", "num_ctas"):
+            if getattr(self, name) < 0:
+                raise ValueError(f"{name} must be non-negative")
+
+    def to_c(self) -> _lib.KairoSpmmConfig:
+        c = _lib.KairoSpmmConfig()
+        c.kernel = {"auto": _lib.KERNEL_AUTO, "simt": _lib.KERNEL_SIMT, "tcgen05": _lib.KERNEL_TCGEN05}[self.kernel]
+        c.n_tile = self.n_tile
+        c.stages = self.stages
+        c.row_cost = self.row_cost
+        c.num_ctas = self.num_ctas
+        return c
+
+
+def _require_cuda(*tensors: Tensor, op: str) -> None:
+    for t in tensors:
+        if not t.is_cuda:
+            raise RuntimeError(f"kairo_b200.{op} runs on CUDA tensors only (got a {t.device} tensor); "
+                               "this package has no CPU implementation")
+
+
+def _dense_to_block_sparse(
+    matrix: Tensor,
+    block_mask: SparseMask,
+    tile_size: int,
+) -> tuple[Tensor, Tensor, Tensor]:
+    """Dense matrix + tile mask -> (A_tiles, tile_row_ids, tile_col_ids).
+
+    Same result as the reference (kairo/ops/spmm.py:16-55): tiles in mask
+    order, zero-padded where a tile crosses the matrix edge, ids as int32.
+    The tiles are gathered on the device by ``kairo_dense_to_tiles``.
+    """
+    _require_cuda(matrix, op="_dense_to_block_sparse")
+    rows = block_mask.indices[0].to(device=matrix.device, dtype=torch.int32).contiguous()
+    cols = block_mask.indices[1].to(device=matrix.device, dtype=torch.int32).contiguous()
+    num_tiles = block_mask.nnz
+    tiles = torch.empty(num_tiles, tile_size, tile_size, dtype=matrix.dtype, device=matrix.device)
+    if num_tiles:
+        a = matrix if matrix.stride(1) == 1 else matrix.contiguous()
+        with torch.cuda.device(matrix.device):
+            _lib.check(_lib.lib().kairo_dense_to_tiles(
+                a.data_ptr(), a.shape[0], a.shape[1], a.stride(0), rows.data_ptr(), cols.data_ptr(), num_tiles,
+                tile_size, _lib.kairo_dtype(a.dtype), tiles.data_ptr(), _lib.stream_handle(matrix.device)),
+                "_dense_to_block_sparse")
+    return tiles, rows, cols
+
+
+def block_sparse_mm(
+    A: Tensor,
+    B: Tensor,
+    block_mask: SparseMask,
+    tile_size: int = 16,
+) -> Tensor:
+    """Block-sparse matrix multiply: C = blocksparse(A) @ B.
+
+    Only the tiles named by ``block_mask`` are read from A.  Mirrors the
+    reference operator (kairo/ops/spmm.py:58-105) on CUDA tensors:
+    raises ``ValueError("Inner dimensions must match: ...")`` on a K mismatch,
+    returns zeros of A's dtype for an empty mask, and otherwise returns the
+    fp32 product computed by the B200 kernels.
+
+    Args:
+        A: dense (M, K) matrix on a CUDA device.
+        B: dense (K, N) matrix on the same device, same dtype as A.
+        block_mask: SparseMask with tile-granular indices.
+        tile_size: tile side length (default 16).
+    """
+    M, K = A.shape
+    K2, N = B.shape
+    if K != K2:
+        raise ValueError(f"Inner dimensions must match: A is ({M}, {K}), B is ({K2}, {N})")
+    _require_cuda(A, B, op="block_sparse_mm")
+    A_tiles, tile_row_ids, tile_col_ids = _dense_to_block_sparse(A, block_mask, tile_size)
+    num_tiles = A_tiles.shape[0]
+    if num_tiles == 0:
+        return torch.zeros(M, N, dtype=A.dtype, device=A.device)
+    return _C.acc_spmm_forward(
+        A_tiles.contiguous(),
+        tile_row_ids.contiguous(),
+        tile_col_ids.contiguous(),
+        B.contiguous(),
+        M, K, N, num_tiles, tile_size, tile_size,
+    )
+
+
+def bsr_from_tiles(
+    tiles: Tensor,
+    tile_row_ids: Tensor,
+    tile_col_ids: Tensor,
+    shape: tuple[int, int],
+) -> BlockSparseMatrix:
+    """Builds a BlockSparseMatrix from a COO tile list, on the device.
+
+    The block order is the reference's stable row sort
+    (kairo/ops/sparse_embedding.py:49-56) with row offsets as in
+    sparse_embedding.py:23-46; ``tiles`` stay where they are and ``blk_idx``
+    maps BSR positions to them (``None`` when the list was already sorted).
+    """
+    _require_cuda(tiles, tile_row_ids, tile_col_ids, op="bsr_from_tiles")
+    if tiles.dim() != 3:
+        raise ValueError("tiles must be (num_tiles, bm, bk)")
+    m, k = shape
+    bm, bk = int(tiles.shape[1]), int(tiles.shape[2])
+    nbr = (m + bm - 1) // bm
+    nbc = (k + bk - 1) // bk
+    nt = int(tiles.shape[0])
+    dev = tiles.device
+    rows = tile_row_ids.to(dtype=torch.int32).contiguous()
+    cols = tile_col_ids.to(dtype=torch.int32).contiguous()
+    if rows.numel() != nt or cols.numel() != nt:
+        raise ValueError("tile id arrays must have one entry per tile")
+    lib = _lib.lib()
+    with torch.cuda.device(dev):
+        row_ptr = torch.empty(nbr + 1, dtype=torch.int32, device=dev)
+        col_idx = torch.empty(nt, dtype=torch.int32, device=dev)
+        perm = torch.empty(nt, dtype=torch.int32, device=dev)
+        nbytes = ctypes.c_size_t(0)
+        _lib.check(lib.kairo_bsr_build_workspace_size(nt, nbr, ctypes.byref(nbytes)), "bsr_from_tiles")
+        ws = torch.empty(max(nbytes.value, 256), dtype=torch.uint8, device=dev)
+        ident = ctypes.c_int32(0)
+        _lib.check(lib.kairo_bsr_build(rows.data_ptr() if nt else None, cols.data_ptr() if nt else None, nt, nbr,
+                                       nbc, row_ptr.data_ptr(), col_idx.data_ptr() if nt else None,
+                                       perm.data_ptr() if nt else None, ctypes.byref(ident), ws.data_ptr(),
+                                       ws.numel(), _lib.stream_handle(dev)), "bsr_from_tiles")
+    return BlockSparseMatrix(row_ptr=row_ptr, col_idx=col_idx, blocks=tiles.contiguous(), shape=(m, k),
+                             block_size=(bm, bk), blk_idx=None if ident.value else perm)
+
+
+def bsr_from_mask(A: Tensor, block_mask: SparseMask, tile_size: int) -> BlockSparseMatrix:
+    """Dense A + tile mask -> BlockSparseMatrix (tiles gathered on the device)."""
+    tiles, rows, cols = _dense_to_block_sparse(A, block_mask, tile_size)
+    return bsr_from_tiles(tiles, rows, cols, (A.shape[0], A.shape[1]))
+
+
+def _bsr_desc(a: BlockSparseMatrix) -> _lib.KairoBsr:
+    d = _lib.KairoBsr()
+    d.rows, d.cols = a.shape
+    d.bm, d.bk = a.block_size
+    d.nbr = a.nbr
+    d.nnzb = a.nnzb
+    d.nblocks_stored = int(a.blocks.shape[0])
+    d.row_ptr = a.row_ptr.data_ptr()
+    d.col_idx = a.col_idx.data_ptr() if a.nnzb else None
+    d.blk_idx = a.blk_idx.data_ptr() if a.blk_idx is not None and a.nnzb else None
+    d.blocks = a.blocks.data_ptr() if a.blocks.numel() else None
+    d.dtype = _lib.kairo_dtype(a.dtype)
+    return d
+
+
+def _launch(a: BlockSparseMatrix, b: Tensor, ldb: int, layout: int, n: int, out: Tensor, ldc: int,
+            config: KernelConfig | None, check_device: bool) -> None:
+    lib = _lib.lib()
+    desc = _bsr_desc(a)
+    cfg = (config or KernelConfig()).to_c()
+    dev = a.device
+    with torch.cuda.device(dev):
+        nbytes = ctypes.c_size_t(0)
+        _lib.check(lib.kairo_bsr_spmm_workspace_size(ctypes.byref(desc), layout, n, ctypes.byref(cfg),
+                                                     ctypes.byref(nbytes)), "kairo_bsr_spmm")
+        ws = _lib.workspace(nbytes.value, dev)
+        _lib.check(lib.kairo_bsr_spmm(ctypes.byref(desc), b.data_ptr(), ldb, layout, n, out.data_ptr(), ldc,
+                                      _lib.kairo_dtype(out.dtype), ctypes.byref(cfg), ws.data_ptr(), ws.numel(),
+                                      _lib.stream_handle(dev)), "kairo_bsr_spmm")
+        if check_device:
+            _lib.raise_on_device_error(ws)
+
+
+def block_sparse_mm_bsr(
+    a: BlockSparseMatrix,
+    B: Tensor,
+    *,
+    out: Tensor | None = None,
+    config: KernelConfig | None = None,
+    check: bool = False,
+) -> Tensor:
+    """C = A_bsr @ B in fp32 (B: (K, N), same dtype as the blocks).
+
+    Every element of C is written.  ``check=True`` synchronises and raises
+    :class:`~kairo_b200._lib.KairoDeviceError` if the device recorded an
+    error (an out-of-range block index or a pipeline wait that timed out).
+    """
+    _require_cuda(a.blocks, B, op="block_sparse_mm_bsr")
+    m, k = a.shape
+    if B.dim() != 2 or B.shape[0] != k:
+        raise ValueError(f"Inner dimensions must match: A is ({m}, {k}), B is {tuple(B.shape)}")
+    if B.dtype != a.dtype:
+        raise TypeError(f"B dtype {B.dtype} differs from block dtype {a.dtype}")
+    if B.stride(1) != 1:
+        B = B.contiguous()
+    n = B.shape[1]
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.float32, device=B.device)
+    elif out.shape != (m, n) or out.dtype != torch.float32 or out.stride(1) != 1:
+        raise ValueError("out must be a row-major (M, N) float32 tensor")
+    _launch(a, B, B.stride(0), _lib.LAYOUT_STANDARD, n, out, out.stride(0), config, check)
+    return out
+
+
+def sparse_linear(
+    X: Tensor,
+    W: BlockSparseMatrix,
+    *,
+    out_dtype: torch.dtype | None = None,
+    out: Tensor | None = None,
+    config: KernelConfig | None = None,
+    check: bool = False,
+) -> Tensor:
+    """Y = X @ W^T for a block-sparse weight W (out_features x in_features).
+
+    X: (batch, in_features), same dtype as W's blocks.  Y: (batch,
+    out_features) in ``out_dtype`` (default: X's dtype), accumulated in fp32
+    and rounded once.  This is ``block_sparse_mm`` with B = X^T and C = Y^T,
+    computed without transposing X or Y.
+    """
+    _require_cuda(W.blocks, X, op="sparse_linear")
+    m, k = W.shape
+    if X.dim() != 2 or X.shape[1] != k:
+        raise ValueError(f"Inner dimensions must match: X is {tuple(X.shape)}, W is ({m}, {k})")
+    if X.dtype != W.dtype:
+        raise TypeError(f"X dtype {X.dtype} differs from weight dtype {W.dtype}")
+    if X.stride(1) != 1:
+        X = X.contiguous()
+    n = X.shape[0]
+    odt = out_dtype or X.dtype
+    if out is None:
+        out = torch.empty(n, m, dtype=odt, device=X.device)
+    elif out.shape != (n, m) or out.stride(1) != 1:
+        raise ValueError("out must be a row-major (batch, out_features) tensor")
+    _launch(W, X, X.stride(0), _lib.LAYOUT_LINEAR, n, out, out.stride(0), config, check)
+    return out
