@@ -98,10 +98,11 @@ typedef struct kairo_bsr {
 typedef struct kairo_spmm_config {
   int32_t kernel;            /* kairo_kernel */
   int32_t n_tile;            /* C columns per work item on tcgen05: 128 or 256 (0 = auto) */
-  int32_t stages;            /* shared-memory pipeline depth (0 = auto) */
+  int32_t stages;            /* pipeline stages in shared memory (0 = auto) */
   int32_t row_cost;          /* scheduler weight of one block-row in units of one block (0 = auto) */
   int32_t num_ctas;          /* persistent grid size (0 = one CTA per SM) */
-  int32_t reserved[3];
+  int32_t group_blocks;      /* nonzero blocks per pipeline stage, 1..32 (0 = auto) */
+  int32_t reserved[2];
 } kairo_spmm_config;
 
 /* Operand layouts of kairo_bsr_spmm. */

@@ -75,7 +75,8 @@ class KairoSpmmConfig(Structure):
         ("stages", c_int32),
         ("row_cost", c_int32),
         ("num_ctas", c_int32),
-        ("reserved", c_int32 * 3),
+        ("group_blocks", c_int32),
+        ("reserved", c_int32 * 2),
     ]
 
 

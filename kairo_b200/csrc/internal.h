@@ -41,7 +41,10 @@ struct TcPlan {
   int row_cost;            // R
   int64_t w;               // path length of one chunk: nnzb + R * nbr
   int grid;                // persistent CTAs
-  int stages;
+  int stages;              // stage groups
+  int group;               // blocks per stage group
+  int nacc;                // independent TMEM accumulators per row piece
+  uint32_t tmem_cols;      // TMEM columns allocated per CTA
   size_t smem_bytes;
   size_t counters_offset, counters_bytes;
   size_t partials_offset, partials_bytes;

@@ -18,12 +18,6 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
@@ -43,6 +37,12 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// Adds `bytes` to the transaction count of the current phase (no arrival).
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -58,23 +58,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits until the phase with parity `parity` of `bar` has completed.  The
-// wait is bounded: after `timeout_ns` of global time it records
+// wait is bounded: after `timeout_cycles` SM clock cycles it records
 // KAIRO_DEVERR_WAIT_TIMEOUT | (tag << 8) in *err, raises *abort_flag and
-// returns false.  It also returns false as soon as another warp of the CTA
-// has raised *abort_flag, so one failed wait stops the whole CTA instead of
-// leaving its other warps spinning.
+// returns false.  It also returns false once another warp of the CTA has
+// raised *abort_flag, so one failed wait stops the whole CTA instead of
+// leaving its other warps spinning.  The fast path is a single try_wait; the
+// clock and the flag are only read while the wait is actually blocked.
 __device__ __forceinline__ bool wait_parity(uint64_t* bar, uint32_t parity,
                                             volatile int* abort_flag, unsigned* err,
-                                            uint32_t tag, uint64_t timeout_ns) {
+                                            uint32_t tag, long long timeout_cycles) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 0;; ++it) {
+  const long long t0 = clock64();
+  for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if ((it & 63u) == 63u && globaltimer_ns() - t0 > timeout_ns) {
-      atomicCAS(err, 0u, KAIRO_DEVERR_WAIT_TIMEOUT | (tag << 8));
-      *abort_flag = 1;
-      return false;
+    if ((it & 15u) == 0u) {
+      if (*abort_flag) return false;
+      if (clock64() - t0 > timeout_cycles) {
+        atomicCAS(err, 0u, KAIRO_DEVERR_WAIT_TIMEOUT | (tag << 8));
+        *abort_flag = 1;
+        return false;
+      }
     }
   }
 }
@@ -104,6 +107,16 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, in
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::"
       "cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// 3D variant (x innermost).  No multicast.
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, int32_t x, int32_t y, int32_t z,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::"
+      "cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
 

@@ -51,7 +51,7 @@ namespace kairo {
 namespace {
 
 constexpr int kThreads = 192;
-constexpr uint64_t kTimeoutNs = 4000000000ull;  // 4 s of global time per wait
+constexpr long long kWaitCycles = 8000000000LL;  // per-wait bound in SM cycles (about 4 s at 2 GHz)
 constexpr int kMaxSmem = 227 * 1024;
 
 // Wait-site tags recorded with a timeout (bits 8..15 of the error word).
@@ -78,8 +78,12 @@ struct TcArgs {
   int32_t chunk_group;
   int32_t ngroups;
   int32_t row_cost;
-  int32_t stages;
+  int32_t stages;          // stage groups in the shared-memory ring
+  int32_t group;           // blocks per stage group
+  int32_t nacc;            // independent accumulators per row piece (1..4)
+  uint32_t tmem_cols;      // TMEM columns allocated (power of two, >= 2*nacc*NT*BM)
   int32_t vec_store;       // LINEAR: rows of Y may be written with 16-byte stores
+  int32_t b_box3d;         // STANDARD: the whole B panel is one 3D box (N % 64 == 0)
 };
 
 struct RowItem {
@@ -272,21 +276,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int PANEL_BYTES = NT * 128 * BK * 2;
   constexpr int A_BYTES = BM * BK * 2;
   constexpr int A_BYTES_PAD = (A_BYTES + 1023) / 1024 * 1024;
-  constexpr int STAGE_BYTES = PANEL_BYTES + A_BYTES_PAD;
+  constexpr int SLOT_BYTES = PANEL_BYTES + A_BYTES_PAD;  // one block + its B panel
   constexpr uint32_t TX_BYTES = PANEL_BYTES + A_BYTES;
-  constexpr int ACC_COLS = NT * BM;
-  constexpr uint32_t TMEM_COLS = (2 * ACC_COLS <= 32) ? 32 : (2 * ACC_COLS <= 64) ? 64
-                                 : (2 * ACC_COLS <= 128) ? 128 : (2 * ACC_COLS <= 256) ? 256 : 512;
+  constexpr int ACC_COLS = NT * BM;  // one accumulator: NT sub-tiles of BM fp32 columns
   constexpr uint32_t IDESC = ptx::make_idesc_f16(IN_FMT, LINEAR ? 0u : 1u, 0u, 128u, BM);
   constexpr uint32_t SW_ROW = ptx::swizzle_code_for_row_bytes(BK * 2);
   constexpr int PART_ELEMS = NT * BM * 128;
   static_assert(BK % 16 == 0 && BM % 16 == 0 && BM <= 256, "block shape");
   static_assert(2 * ACC_COLS <= 512, "TMEM budget");
+  const int NACC = args.nacc;                 // accumulators per TMEM slot
+  const uint32_t TMEM_COLS = args.tmem_cols;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = args.stages;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * STAGE_BYTES);
+  const int GB = args.group;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * GB * SLOT_BYTES);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
   uint64_t* tempty = tfull + 2;
@@ -295,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 0);
   volatile int* abort_flag = misc + 1;
   int* red_flag = misc + 3;
-  int* issued = misc + 4;  // [S]: parity+1 of the last load issued into each stage
+  int* issued = misc + 4;  // [S]: parity+1 of the last group loaded into each stage
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -341,10 +346,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
+    // Blocks are loaded in groups of GB consecutive blocks per stage: one
+    // lane per block issues that block's two TMA loads, so a whole group is
+    // issued by a couple of warp instructions, and the group's full barrier
+    // gets a single arrival once every block of it has its expect_tx.
     const uint64_t pol_a = ptx::policy_evict_first();
     const uint64_t pol_b = ptx::policy_evict_last();
-    int stage = 0;
-    uint32_t phase = 0;
+    int gpos = 0;      // next slot in the current group
+    int gidx = 0;      // stage of the current group
+    uint32_t gph = 0;  // phase of that stage
     walk_items(args, s_range, e_range, i_start, lane, [&](const RowItem& it) -> bool {
       if (it.kind != kDirect && it.kind != kPartial) return true;
       const int n0 = it.chunk * NT * 128;
@@ -361,93 +371,122 @@ __global__ void __launch_bounds__(kThreads, 1)
             mb = 0;
           }
         }
-        for (int q = 0; q < cnt; ++q) {
-          const int c = __shfl_sync(0xffffffffu, mc, q);
-          const int blk = __shfl_sync(0xffffffffu, mb, q);
-          int ok = 1;
-          if (lane == 0) {
-            ok = ptx::wait_parity(&empty[stage], phase ^ 1u, abort_flag, args.err, kTagEmpty, kTimeoutNs);
-            if (ok) {
-              uint8_t* st = smem + stage * STAGE_BYTES;
-              ptx::mbar_arrive_expect_tx(&full[stage], TX_BYTES);
-              ptx::tma_load_2d(st + PANEL_BYTES, &tmap_a, 0, blk * BM, &full[stage], pol_a);
-              if (!LINEAR) {
+        int j0 = 0;
+        while (j0 < cnt) {
+          const int take = min(GB - gpos, cnt - j0);
+          if (gpos == 0) {
+            int ok = 1;
+            if (lane == 0) {
+              ok = ptx::wait_parity(&empty[gidx], gph ^ 1u, abort_flag, args.err, kTagEmpty, kWaitCycles);
+              if (ok) issued[gidx] = static_cast<int>(gph) + 1;
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) return false;
+          }
+          if (lane >= j0 && lane < j0 + take) {
+            uint8_t* st = smem + (gidx * GB + gpos + (lane - j0)) * SLOT_BYTES;
+            ptx::mbar_expect_tx(&full[gidx], TX_BYTES);
+            ptx::tma_load_2d(st + PANEL_BYTES, &tmap_a, 0, mb * BM, &full[gidx], pol_a);
+            if (LINEAR) {
+              // X rows n0 .. n0+128*NT as one box: sub-tile t lands at t*128*BK*2.
+              ptx::tma_load_2d(st, &tmap_b, mc * BK, n0, &full[gidx], pol_b);
+            } else if (args.b_box3d) {
+              // B viewed as [N/64][K][64]: the 2*NT column atoms of the
+              // panel arrive as [atom][k][64] in one box.
+              ptx::tma_load_3d(st, &tmap_b, 0, mc * BK, n0 / 64, &full[gidx], pol_b);
+            } else {
 #pragma unroll
-                for (int h = 0; h < 2 * NT; ++h)
-                  ptx::tma_load_2d(st + h * BK * 128, &tmap_b, n0 + 64 * h, c * BK, &full[stage], pol_b);
-              } else {
-#pragma unroll
-                for (int t = 0; t < NT; ++t)
-                  ptx::tma_load_2d(st + t * 128 * BK * 2, &tmap_b, c * BK, n0 + 128 * t, &full[stage], pol_b);
-              }
-              issued[stage] = static_cast<int>(phase) + 1;
+              for (int h = 0; h < 2 * NT; ++h)
+                ptx::tma_load_2d(st + h * BK * 128, &tmap_b, n0 + 64 * h, mc * BK, &full[gidx], pol_b);
             }
           }
-          ok = __shfl_sync(0xffffffffu, ok, 0);
-          if (!ok) return false;
-          if (++stage == S) {
-            stage = 0;
-            phase ^= 1u;
+          __syncwarp();
+          gpos += take;
+          j0 += take;
+          if (gpos == GB) {
+            if (lane == 0) ptx::mbar_arrive(&full[gidx]);
+            gpos = 0;
+            if (++gidx == S) {
+              gidx = 0;
+              gph ^= 1u;
+            }
           }
         }
       }
       return true;
     });
+    // Close a partly filled last group (also after an abort, so that the
+    // loads already issued can complete its phase before the drain below).
+    if (gpos != 0 && lane == 0) ptx::mbar_arrive(&full[gidx]);
+    __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    int stage = 0;
-    uint32_t phase = 0;
+    // Lane 0 issues every MMA.  Descriptors are built once and advanced by
+    // adding (byte offset >> 4) to their start-address field.
+    int mpos = 0, midx = 0;
+    uint32_t mph = 0;
     int slot = 0;
     uint32_t aphase = 0;
+    const uint32_t sbase = ptx::smem_u32(smem);
+    const uint64_t adesc0 = LINEAR ? ptx::make_smem_desc(sbase, 16, 8 * BK * 2, SW_ROW)
+                                   : ptx::make_smem_desc(sbase, BK * 128, 1024, 2u);
+    const uint64_t bdesc0 = ptx::make_smem_desc(sbase + PANEL_BYTES, 16, 8 * BK * 2, SW_ROW);
     walk_items(args, s_range, e_range, i_start, lane, [&](const RowItem& it) -> bool {
       if (it.kind != kDirect && it.kind != kPartial) return true;
       int ok = 1;
-      if (lane == 0)
-        ok = ptx::wait_parity(&tempty[slot], aphase ^ 1u, abort_flag, args.err, kTagTmemEmpty, kTimeoutNs);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) return false;
-      ptx::tc_fence_after();
-      const uint32_t d_base = tmem_base + static_cast<uint32_t>(slot * ACC_COLS);
-      for (int p = it.p0; p < it.p1; ++p) {
-        if (lane == 0) {
-          ok = ptx::wait_parity(&full[stage], phase, abort_flag, args.err, kTagFull, kTimeoutNs);
-          if (ok) {
-            ptx::tc_fence_after();
-            const uint32_t st = ptx::smem_u32(smem + stage * STAGE_BYTES);
+      if (lane == 0) {
+        ok = ptx::wait_parity(&tempty[slot], aphase ^ 1u, abort_flag, args.err, kTagTmemEmpty, kWaitCycles);
+        if (ok) {
+          ptx::tc_fence_after();
+          // Consecutive blocks of a row piece go to NACC independent
+          // accumulators, so back-to-back MMAs do not wait on each other's
+          // accumulator update; the epilogue adds the NACC partial sums.
+          const uint32_t slot_base = tmem_base + static_cast<uint32_t>(slot * NACC * ACC_COLS);
+          int acc = 0;
+          for (int p = it.p0; p < it.p1; ++p) {
+            const uint32_t d_base = slot_base + static_cast<uint32_t>(acc * ACC_COLS);
+            const bool first = (p - it.p0) < NACC;
+            if (mpos == 0) {
+              ok = ptx::wait_parity(&full[midx], mph, abort_flag, args.err, kTagFull, kWaitCycles);
+              if (!ok) break;
+              ptx::tc_fence_after();
+            }
+            const uint64_t off16 = static_cast<uint64_t>(((midx * GB + mpos) * SLOT_BYTES) >> 4);
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk) {
-              const uint64_t bdesc = ptx::make_smem_desc(st + PANEL_BYTES + kk * 32, 16, 8 * BK * 2, SW_ROW);
+              const uint64_t bdesc = bdesc0 + off16 + static_cast<uint64_t>((kk * 32) >> 4);
 #pragma unroll
               for (int t = 0; t < NT; ++t) {
-                uint64_t adesc;
-                if (!LINEAR)
-                  adesc = ptx::make_smem_desc(st + t * 2 * BK * 128 + kk * 2048, BK * 128, 1024, 2u);
-                else
-                  adesc = ptx::make_smem_desc(st + t * 128 * BK * 2 + kk * 32, 16, 8 * BK * 2, SW_ROW);
-                ptx::mma_f16_ss(d_base + t * BM, adesc, bdesc, IDESC, (p > it.p0 || kk > 0) ? 1u : 0u);
+                const uint32_t a_off = LINEAR ? (t * 128 * BK * 2 + kk * 32) : (t * 2 * BK * 128 + kk * 2048);
+                ptx::mma_f16_ss(d_base + t * BM, adesc0 + off16 + (a_off >> 4), bdesc, IDESC,
+                                (!first || kk > 0) ? 1u : 0u);
               }
             }
-            ptx::mma_commit(&empty[stage]);
+            if (++acc == NACC) acc = 0;
+            if (++mpos == GB) {
+              ptx::mma_commit(&empty[midx]);
+              mpos = 0;
+              if (++midx == S) {
+                midx = 0;
+                mph ^= 1u;
+              }
+            }
           }
-        }
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) return false;
-        if (++stage == S) {
-          stage = 0;
-          phase ^= 1u;
+          if (ok) ptx::mma_commit(&tfull[slot]);
         }
       }
-      if (lane == 0) ptx::mma_commit(&tfull[slot]);
-      __syncwarp();
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) return false;
       slot ^= 1;
       if (slot == 0) aphase ^= 1u;
       return true;
     });
     // Every MMA issued above has completed once mma_done flips.
     if (lane == 0) {
+      if (mpos != 0) ptx::mma_commit(&empty[midx]);
       ptx::mma_commit(mma_done);
       int dummy = 0;
-      ptx::wait_parity(mma_done, 0, reinterpret_cast<volatile int*>(&dummy), args.err, kTagDrain, kTimeoutNs);
+      ptx::wait_parity(mma_done, 0, reinterpret_cast<volatile int*>(&dummy), args.err, kTagDrain, kWaitCycles);
     }
     __syncwarp();
   } else {
@@ -471,20 +510,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       int ok = 1;
       if (lane == 0)
-        ok = ptx::wait_parity(&tfull[slot], aphase, abort_flag, args.err, kTagTmemFull, kTimeoutNs);
+        ok = ptx::wait_parity(&tfull[slot], aphase, abort_flag, args.err, kTagTmemFull, kWaitCycles);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (epi_any(!ok)) return false;
       ptx::tc_fence_after();
       float* part = nullptr;
       if (it.kind == kPartial)
         part = args.partials + (static_cast<int64_t>(it.group * G + blockIdx.x) * 2 + it.slot) * PART_ELEMS;
+      const int nsum = min(NACC, it.p1 - it.p0);  // accumulators this piece wrote
+      const uint32_t slot_cols = static_cast<uint32_t>(slot * NACC * ACC_COLS);
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
 #pragma unroll
         for (int j0 = 0; j0 < BM; j0 += 16) {
-          float v[16];
-          ptx::tmem_ld16(tmem_base + lane_addr + static_cast<uint32_t>(slot * ACC_COLS + t * BM + j0), v);
+          float v[16], w1[16], w2[16], w3[16];
+          const uint32_t col = tmem_base + lane_addr + slot_cols + static_cast<uint32_t>(t * BM + j0);
+          ptx::tmem_ld16(col, v);
+          if (nsum > 1) ptx::tmem_ld16(col + ACC_COLS, w1);
+          if (nsum > 2) ptx::tmem_ld16(col + 2 * ACC_COLS, w2);
+          if (nsum > 3) ptx::tmem_ld16(col + 3 * ACC_COLS, w3);
           ptx::tmem_wait_ld();
+          if (nsum > 1) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) v[jj] += w1[jj];
+          }
+          if (nsum > 2) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) v[jj] += w2[jj];
+          }
+          if (nsum > 3) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) v[jj] += w3[jj];
+          }
           if (it.kind == kDirect) {
             store16<LINEAR, TOut>(args, it.row, BM, j0, n0 + t * 128 + e, v);
           } else {
@@ -538,7 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < S; ++s)
       if (issued[s])
         ptx::wait_parity(&full[s], static_cast<uint32_t>(issued[s] - 1), reinterpret_cast<volatile int*>(&dummy),
-                         args.err, kTagDrain, kTimeoutNs);
+                         args.err, kTagDrain, kWaitCycles);
   }
   __syncthreads();
   if (warp == 1) {
@@ -587,6 +644,26 @@ kairo_status make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
   if (r != CUDA_SUCCESS) {
     std::ostringstream os;
     os << "cuTensorMapEncodeTiled failed for " << what << " (CUresult " << static_cast<int>(r) << ")";
+    return fail(KAIRO_STATUS_INVALID_VALUE, os.str());
+  }
+  return KAIRO_STATUS_SUCCESS;
+}
+
+// B (K x N, row stride ldb) viewed as [N/64][K][64] so that one box of
+// (64, bk, atoms) brings a whole panel in the MN-major 128B-swizzled layout.
+kairo_status make_map_b3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t n, uint64_t k,
+                          uint64_t ldb, uint32_t bk, uint32_t atoms) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(KAIRO_STATUS_CUDA_ERROR, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[3] = {64, k, n / 64};
+  const cuuint64_t strides[2] = {ldb * 2, 128};
+  const cuuint32_t box[3] = {64, bk, atoms};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    std::ostringstream os;
+    os << "cuTensorMapEncodeTiled failed for the 3D view of B (CUresult " << static_cast<int>(r) << ")";
     return fail(KAIRO_STATUS_INVALID_VALUE, os.str());
   }
   return KAIRO_STATUS_SUCCESS;
@@ -707,14 +784,38 @@ kairo_status tc_plan(const kairo_bsr* a, int32_t layout, int64_t n, const kairo_
   if (grid > L) grid = static_cast<int>(L);
   if (grid < 1) grid = 1;
   p.grid = grid;
+  // Shared memory: `stages` groups of `group` block slots.  Prefer large
+  // groups (fewer pipeline handoffs per block) while keeping >= 4 groups in
+  // flight to cover the load latency.
   const int sb = stage_bytes(p.bm, p.bk, nt);
   const int reserve = 1024 /*alignment*/ + 1024 /*barriers and flags*/;
-  int max_stages = (kMaxSmem - reserve) / sb;
-  if (max_stages > 16) max_stages = 16;
+  const int budget = kMaxSmem - reserve;
+  int group = (cfg && cfg->group_blocks > 0) ? cfg->group_blocks : 0;
+  if (group > 32) return fail(KAIRO_STATUS_INVALID_VALUE, "group_blocks must be at most 32");
+  if (group == 0) {
+    const int cand[] = {8, 6, 4, 3, 2, 1};
+    group = 1;
+    for (int g : cand)
+      if (budget / (g * sb) >= 4) {
+        group = g;
+        break;
+      }
+  }
+  int max_stages = budget / (group * sb);
+  if (max_stages > 32) max_stages = 32;
   int stages = (cfg && cfg->stages > 0) ? std::min(cfg->stages, max_stages) : max_stages;
   if (stages < 2) return fail(KAIRO_STATUS_NOT_SUPPORTED, "shared memory too small for two pipeline stages");
+  p.group = group;
   p.stages = stages;
-  p.smem_bytes = static_cast<size_t>(stages) * sb + reserve;
+  // Up to four accumulators per TMEM slot, two slots, within 512 columns.
+  int nacc = 512 / (2 * nt * p.bm);
+  if (nacc > 4) nacc = 4;
+  if (nacc < 1) nacc = 1;
+  p.nacc = nacc;
+  const int need = 2 * nacc * nt * p.bm;
+  p.tmem_cols = 32;
+  while (p.tmem_cols < static_cast<uint32_t>(need)) p.tmem_cols <<= 1;
+  p.smem_bytes = static_cast<size_t>(stages) * group * sb + reserve;
   p.counters_offset = kWorkspaceHeaderBytes;
   p.counters_bytes = kCounterRegionBytes;
   p.partials_offset = p.counters_offset + p.counters_bytes;
@@ -736,12 +837,21 @@ kairo_status tc_launch(const kairo_bsr* a, const void* b, int64_t ldb, int32_t l
                                 static_cast<uint64_t>(a->nblocks_stored) * a->bm, static_cast<uint64_t>(a->bk),
                                 static_cast<uint32_t>(a->bk), static_cast<uint32_t>(a->bm), "block storage");
   if (st) return st;
-  if (!linear)
-    st = make_map_2d(&map_b, b, dt, 2, static_cast<uint64_t>(n), static_cast<uint64_t>(a->cols),
-                     static_cast<uint64_t>(ldb), 64, static_cast<uint32_t>(a->bk), "B");
-  else
+  int b_box3d = 0;
+  if (!linear) {
+    if (n % 64 == 0) {
+      st = make_map_b3d(&map_b, b, dt, static_cast<uint64_t>(n), static_cast<uint64_t>(a->cols),
+                        static_cast<uint64_t>(ldb), static_cast<uint32_t>(a->bk), static_cast<uint32_t>(2 * plan.nt));
+      b_box3d = (st == KAIRO_STATUS_SUCCESS);
+    }
+    if (!b_box3d)
+      st = make_map_2d(&map_b, b, dt, 2, static_cast<uint64_t>(n), static_cast<uint64_t>(a->cols),
+                       static_cast<uint64_t>(ldb), 64, static_cast<uint32_t>(a->bk), "B");
+  } else {
     st = make_map_2d(&map_b, b, dt, 2, static_cast<uint64_t>(a->cols), static_cast<uint64_t>(n),
-                     static_cast<uint64_t>(ldb), static_cast<uint32_t>(a->bk), 128, "X");
+                     static_cast<uint64_t>(ldb), static_cast<uint32_t>(a->bk), static_cast<uint32_t>(128 * plan.nt),
+                     "X");
+  }
   if (st) return st;
 
   TcArgs args{};
@@ -767,7 +877,11 @@ kairo_status tc_launch(const kairo_bsr* a, const void* b, int64_t ldb, int32_t l
   args.ngroups = plan.ngroups;
   args.row_cost = plan.row_cost;
   args.stages = plan.stages;
+  args.group = plan.group;
+  args.nacc = plan.nacc;
+  args.tmem_cols = plan.tmem_cols;
   const size_t osz = elem_size(c_dtype);
+  args.b_box3d = b_box3d;
   args.vec_store = linear && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0) && ((ldc * osz) % 16 == 0) ? 1 : 0;
 
   cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,

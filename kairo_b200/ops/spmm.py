@@ -28,9 +28,10 @@ class KernelConfig:
     """Launch knobs of the BSR SpMM (0 = library default).
 
     kernel: "auto", "simt" or "tcgen05"; n_tile: C columns per work item on
-    the tcgen05 kernel (128 or 256); stages: shared-memory pipeline depth;
-    row_cost: scheduler weight of a block-row in units of one block;
-    num_ctas: persistent grid size.
+    the tcgen05 kernel (128 or 256); stages: pipeline stages in shared
+    memory; row_cost: scheduler weight of a block-row in units of one block;
+    num_ctas: persistent grid size; group_blocks: nonzero blocks loaded per
+    pipeline stage (1..32).
     """
 
     kernel: str = "auto"
@@ -38,15 +39,18 @@ class KernelConfig:
     stages: int = 0
     row_cost: int = 0
     num_ctas: int = 0
+    group_blocks: int = 0
 
     def __post_init__(self) -> None:
         if self.kernel not in ("auto", "simt", "tcgen05"):
             raise ValueError(f"kernel must be 'auto', 'simt' or 'tcgen05', got {self.kernel!r}")
         if self.n_tile not in (0, 128, 256):
             raise ValueError(f"n_tile must be 0, 128 or 256, got {self.n_tile}")
-        for name in ("stages", "row_cost", "num_ctas"):
+        for name in ("stages", "row_cost", "num_ctas", "group_blocks"):
             if getattr(self, name) < 0:
                 raise ValueError(f"{name} must be non-negative")
+        if self.group_blocks > 32:
+            raise ValueError("group_blocks must be at most 32")
 
     def to_c(self) -> _lib.KairoSpmmConfig:
         c = _lib.KairoSpmmConfig()
@@ -55,6 +59,7 @@ class KernelConfig:
         c.stages = self.stages
         c.row_cost = self.row_cost
         c.num_ctas = self.num_ctas
+        c.group_blocks = self.group_blocks
         return c
 
 
