@@ -1,0 +1,479 @@
+"""Benchmark of the B200 BSR SpMM (C = A_bsr @ B).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload NAME] [--gather]
+
+One process per GPU (torchrun for N > 1).  A is sharded by nnz-balanced
+block-row ranges, B is replicated, and no collective runs on the compute path.
+Every rank generates the same seeded workload on its device and keeps its own
+shard.  A step is one SpMM launch over the local shard.  It is timed with CUDA
+events on the launching stream.  The L2 is flushed before every step by
+writing a 256 MiB buffer, which is not timed.  The job's time is the max over
+ranks.  Rank 0 prints one JSON line.
+
+The default workload is ``bf16_uniform``: A is 262144 x 262144 bf16 with
+32x32 blocks and 99.5 % block sparsity, B is 262144 x 1024, and C is fp32.
+It is the configuration defined at 1, 2, 4 and 8 GPUs, so per-N values are
+comparable (strong scaling: the total work is fixed).
+
+``--impl reference`` times the CPU restatement of the reference's SpMM path
+(oracle/, multi-threaded) on rank 0 over a bounded sample of the same
+workload.  Other ranks exit without work.
+"""
+
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from kairo_b200.workloads import WORKLOADS, canonical_bytes, flops, generate, strict_bytes  # noqa: E402
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def log(*a) -> None:
+    print(*a, file=sys.stderr, flush=True)
+
+
+def measured_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except Exception:  # noqa: BLE001
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def dist_env() -> tuple[int, int, int]:
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during a region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device) -> None:
+        # nvidia-smi numbers GPUs physically; select ours by UUID.
+        try:
+            self.sel = ["-i", "GPU-" + str(torch.cuda.get_device_properties(device).uuid)]
+        except Exception:  # noqa: BLE001
+            self.sel = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "50", *self.sel], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self) -> dict:
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for row in csv.reader(io.StringIO(getattr(self, "out", "") or "")):
+            if len(row) < 9:
+                continue
+            try:
+                sms.append(float(row[1]))
+                maxes.append(float(row[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, row[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxes), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+def load_traffic(workload: str) -> float | None:
+    """DRAM bytes per launch of the SpMM kernel for the full single-GPU
+    workload, from the committed ncu summary (profiles/traffic_<workload>.txt)."""
+    p = ROOT / "profiles" / f"traffic_{workload}.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1])
+            except ValueError:
+                return None
+    return None
+
+
+def workload_spec(args):
+    spec = WORKLOADS[args.workload]
+    if args.shape:
+        m, k, n = (int(x) for x in args.shape.lower().split("x"))
+        spec = spec.scaled(m, k, n)
+    return spec
+
+
+# ---------------------------------------------------------------- CPU sample
+
+def cpu_sample(problem, bsr_host, target_s: float, nthreads: int = 0):
+    """Times the oracle (the reference's CPU algorithm, multi-threaded) on the
+    first block-rows of the workload, sized for about ``target_s`` seconds.
+    Returns (TFLOP/s, seconds, description)."""
+    from oracle import oracle
+
+    row_ptr, col_idx, blocks, b = bsr_host
+    spec = problem.spec
+    nbr = row_ptr.numel() - 1
+    threads = nthreads or oracle.num_threads()
+    # calibrate on a few rows
+    rows = list(range(min(nbr, max(threads, 8))))
+    t0 = time.perf_counter()
+    oracle.spmm_bsr_rows(row_ptr, col_idx, None, blocks, b, spec.m, spec.k, spec.n, rows, nthreads=threads)
+    dt = max(time.perf_counter() - t0, 1e-4)
+    per_row = dt / len(rows)
+    nrows = int(min(nbr, max(len(rows), target_s / per_row)))
+    rows = list(range(nrows))
+    t0 = time.perf_counter()
+    oracle.spmm_bsr_rows(row_ptr, col_idx, None, blocks, b, spec.m, spec.k, spec.n, rows, nthreads=threads)
+    dt = time.perf_counter() - t0
+    nblk = int(row_ptr[nrows].item())
+    fl = 2.0 * nblk * spec.block * spec.block * spec.n
+    desc = (f"block-rows 0..{nrows - 1} of {nbr} ({nblk} of {int(row_ptr[-1].item())} nonzero blocks, "
+            f"{fl / 1e9:.1f} GFLOP), fp32-widened inputs, {threads} threads")
+    return fl / dt / 1e12, dt, desc, threads
+
+
+def host_bsr(problem, a):
+    """CPU copies of a BSR matrix built on the device (for the CPU legs)."""
+    return (a.row_ptr.cpu(), a.col_idx.cpu(), a.blocks.cpu(), problem.b.cpu())
+
+
+# ---------------------------------------------------------------- reference arm
+
+def run_reference(args) -> None:
+    rank, world, local = dist_env()
+    if rank != 0:
+        return
+    spec = workload_spec(args)
+    torch.cuda.set_device(local) if torch.cuda.is_available() else None
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    t0 = time.perf_counter()
+    problem = generate(spec, seed=args.seed, device=dev)
+    from kairo_b200.ops import bsr_from_tiles
+
+    if dev == "cuda":
+        a = bsr_from_tiles(problem.tiles, problem.row_ids, problem.col_ids, (spec.m, spec.k))
+        host = host_bsr(problem, a)
+    else:
+        raise SystemExit("the reference arm needs the workload generated on a CUDA device")
+    log(f"[reference] workload ready in {time.perf_counter() - t0:.1f}s")
+    values, secs = [], []
+    desc, threads = "", 0
+    for i in range(args.warmup + args.steps):
+        v, dt, desc, threads = cpu_sample(problem, host, target_s=args.ref_seconds)
+        if i >= args.warmup:
+            values.append(v)
+            secs.append(dt)
+    value = statistics.median(values)
+    line = {
+        "impl": "reference",
+        "metric": "bsr_spmm_effective_tflops",
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": statistics.median(secs) * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded)",
+        "config": {"workload": spec.name, "m": spec.m, "k": spec.k, "n": spec.n, "block": spec.block,
+                   "sparsity": spec.sparsity, "input_dtype": str(spec.dtype).replace("torch.", ""),
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- our arm
+
+def run_ours(args) -> None:
+    import torch.distributed as dist
+
+    from kairo_b200.ops import KernelConfig, block_sparse_mm_bsr, bsr_from_tiles
+    from kairo_b200.sharding import gather_rows, partition_rows, shard_bsr
+
+    rank, world, local = dist_env()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    spec = workload_spec(args)
+    t0 = time.perf_counter()
+    problem = generate(spec, seed=args.seed, device=dev)
+    a_full = bsr_from_tiles(problem.tiles, problem.row_ids, problem.col_ids, (spec.m, spec.k))
+    bounds = partition_rows(a_full.row_ptr, world)
+    a, shard = shard_bsr(a_full, rank, world, bounds)
+    local_nnzb = a.nnzb
+    local_rows = a.shape[0]
+    b = problem.b
+    cfg = KernelConfig(n_tile=args.n_tile, group_blocks=args.group_blocks)
+    linear = spec.layout == "linear"
+    out_rows = local_rows
+    if linear:
+        from kairo_b200.ops import sparse_linear
+
+        out = torch.empty(spec.n, local_rows, dtype=spec.out_dtype, device=dev)
+
+        def step():
+            sparse_linear(b, a, out=out, config=cfg)
+    else:
+        out = torch.empty(out_rows, spec.n, dtype=torch.float32, device=dev)
+
+        def step():
+            block_sparse_mm_bsr(a, b, out=out, config=cfg)
+    torch.cuda.synchronize()
+    log(f"[rank {rank}] workload {spec.name}: shard rows {shard.row_begin}..{shard.row_end} of {a_full.nbr}, "
+        f"{local_nnzb} blocks, ready in {time.perf_counter() - t0:.1f}s")
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(dev)
+    with sampler:
+        wall0 = time.perf_counter()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - wall0
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]  # ms
+    total_ms = sum(per_step)
+    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    job_ms = t.item()
+    ms_per_step = job_ms / args.steps
+    total_flop = flops(spec)
+    value = total_flop / (ms_per_step / 1e3) / 1e12
+
+    peaks, peak_kind = measured_peaks()
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    local_flop = flops(spec, nnzb=local_nnzb)
+    local_canon = canonical_bytes(spec, nnzb=local_nnzb, nbr=a.nbr, m=local_rows)
+    local_strict = strict_bytes(spec, nnzb=local_nnzb, nbr=a.nbr, m=local_rows)
+    my_ms = total_ms / args.steps
+    achieved = local_canon / (my_ms / 1e3) / 1e9
+    traffic_full = load_traffic(spec.name)
+    traffic = None
+    if traffic_full is not None:
+        traffic = traffic_full * (local_nnzb / max(1, a_full.nnzb))
+    bf16_peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+
+    # Optional replicated output (reported separately, not part of the step).
+    gather_ms = None
+    if args.gather and world > 1 and not linear:
+        torch.cuda.synchronize()
+        dist.barrier()
+        g0 = torch.cuda.Event(enable_timing=True)
+        g1 = torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        gather_rows(out, bounds, shard.block_rows, spec.m)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        gt = torch.tensor([g0.elapsed_time(g1)], dtype=torch.float64, device=dev)
+        dist.all_reduce(gt, op=dist.ReduceOp.MAX)
+        gather_ms = gt.item()
+
+    # End to end: host buffers in, the public operator, host result out.
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, spec, a, b, out, cfg, dev, stream, linear, world, dist)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        host = host_bsr(problem, a_full)
+        v, dt, desc, threads = cpu_sample(problem, host, target_s=args.cpu_seconds)
+        cpu = {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": desc}
+
+    clocks = sampler.summary()
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": "bsr_spmm_effective_tflops",
+            "value": value,
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_per_step,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": str(spec.dtype).replace("torch.", ""),
+            "data": "synthetic (seeded, generated on device)",
+            "config": {
+                "workload": spec.name, "m": spec.m, "k": spec.k, "n": spec.n, "block": spec.block,
+                "sparsity": spec.sparsity, "nnzb": a_full.nnzb, "out_dtype": str(spec.out_dtype).replace("torch.", ""),
+                "parallelism": f"row-shard{world} (nnz-balanced block rows, B replicated)",
+                "l2": "flushed before every step (256 MiB write, untimed)",
+                "kernel_config": {"n_tile": args.n_tile, "group_blocks": args.group_blocks},
+            },
+            "roofline": {
+                "bound": "hbm",
+                "achieved": achieved,
+                "peak": hbm,
+                "unit": "GB/s",
+                "frac": achieved / hbm,
+                "traffic": traffic,
+                "peak_kind": peak_kind,
+                "bytes_definition": "canonical: A blocks + int32 indices + gathered B panel per block + C",
+                "strict_frac": local_strict / (my_ms / 1e3) / 1e9 / hbm,
+                "tensor_frac": local_flop / (my_ms / 1e3) / 1e12 / bf16_peak,
+            },
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "wall_s_timed_region": wall,
+        }
+        if gather_ms is not None:
+            line["gather_ms"] = gather_ms
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_e2e(args, spec, a, b, out, cfg, dev, stream, linear, world, dist):
+    """Same metric through the public operator with host (pinned) buffers:
+    every step copies this rank's blocks, indices and B to the device and
+    reads C back; the copies are inside the timed region."""
+    from kairo_b200.ops import block_sparse_mm_bsr, sparse_linear
+    from kairo_b200.types import BlockSparseMatrix
+
+    h_blocks = a.blocks.to("cpu").pin_memory()
+    h_rp = a.row_ptr.to("cpu").pin_memory()
+    h_ci = a.col_idx.to("cpu").pin_memory()
+    h_b = b.to("cpu").pin_memory()
+    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    d_blocks = torch.empty_like(a.blocks)
+    d_rp = torch.empty_like(a.row_ptr)
+    d_ci = torch.empty_like(a.col_idx)
+    d_b = torch.empty_like(b)
+    steps = max(1, min(args.steps, args.e2e_steps))
+
+    def one():
+        d_blocks.copy_(h_blocks, non_blocking=True)
+        d_rp.copy_(h_rp, non_blocking=True)
+        d_ci.copy_(h_ci, non_blocking=True)
+        d_b.copy_(h_b, non_blocking=True)
+        m = BlockSparseMatrix(row_ptr=d_rp, col_idx=d_ci, blocks=d_blocks, shape=a.shape, block_size=a.block_size)
+        if linear:
+            sparse_linear(d_b, m, out=out, config=cfg)
+        else:
+            block_sparse_mm_bsr(m, d_b, out=out, config=cfg)
+        h_out.copy_(out, non_blocking=True)
+
+    one()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        one()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item()
+    h2d = h_blocks.numel() * h_blocks.element_size() + h_rp.numel() * 4 + h_ci.numel() * 4 + h_b.numel() * h_b.element_size()
+    d2h = h_out.numel() * h_out.element_size()
+    if world > 1:
+        tb = torch.tensor([float(h2d), float(d2h)], dtype=torch.float64, device=dev)
+        dist.all_reduce(tb, op=dist.ReduceOp.SUM)
+        h2d, d2h = int(tb[0].item()), int(tb[1].item())
+    return {"value": flops(spec) / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": steps,
+            "path": "pinned host -> device copies, kairo_b200.ops.block_sparse_mm_bsr, device -> pinned host"}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="bf16_uniform")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--shape", default="", help="MxKxN override of the workload's sizes (same density), "
+                    "for profiling smaller cases")
+    ap.add_argument("--n-tile", type=int, default=0)
+    ap.add_argument("--group-blocks", type=int, default=0)
+    ap.add_argument("--gather", action="store_true", help="also time the all-gather of C (reported separately)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-seconds", type=float, default=3.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        log("warning: fewer than 3 warm-up steps")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

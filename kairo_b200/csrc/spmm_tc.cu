@@ -758,10 +758,10 @@ kairo_status tc_plan(const kairo_bsr* a, int32_t layout, int64_t n, const kairo_
     if (cfg->n_tile != 128 && cfg->n_tile != 256) return fail(KAIRO_STATUS_INVALID_VALUE, "n_tile must be 128 or 256");
     nt = cfg->n_tile / 128;
   } else {
-    // Two sub-tiles halve block re-reads when the B operand stays in L2;
-    // a single 128-column chunk keeps the L2-resident slice of a large B small.
-    const double b_bytes = static_cast<double>(a->cols) * static_cast<double>(n) * 2.0;
-    nt = (n > 128 && (layout == KAIRO_LAYOUT_LINEAR || b_bytes <= 64.0 * 1024 * 1024)) ? 2 : 1;
+    // Two 128-column sub-tiles per work item: each block (the MMA B
+    // operand) is loaded once for 256 columns of C, halving block re-reads
+    // and pipeline handoffs per FLOP.  One sub-tile only when N <= 128.
+    nt = n > 128 ? 2 : 1;
   }
   p.nt = nt;
   p.nchunks = static_cast<int>(ceil_div64(n, 128 * nt));
