@@ -170,8 +170,12 @@ def cpu_sample(problem, bsr_host, target_s: float, nthreads: int = 0):
 
 
 def host_bsr(problem, a):
-    """CPU copies of a BSR matrix built on the device (for the CPU legs)."""
-    return (a.row_ptr.cpu(), a.col_idx.cpu(), a.blocks.cpu(), problem.b.cpu())
+    """CPU copies of a BSR matrix built on the device and of its dense
+    operand as B (K x N); the linear layout's X (N x K) is transposed."""
+    b = problem.b.cpu()
+    if problem.spec.layout == "linear":
+        b = b.t().contiguous()
+    return (a.row_ptr.cpu(), a.col_idx.cpu(), a.blocks.cpu(), b)
 
 
 # ---------------------------------------------------------------- reference arm

@@ -43,7 +43,6 @@ struct TcPlan {
   int grid;                // persistent CTAs
   int stages;              // stage groups
   int group;               // blocks per stage group
-  int nacc;                // independent TMEM accumulators per row piece
   uint32_t tmem_cols;      // TMEM columns allocated per CTA
   size_t smem_bytes;
   size_t counters_offset, counters_bytes;

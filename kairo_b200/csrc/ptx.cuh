@@ -37,6 +37,22 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive_if(uint32_t issue, uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %1, 0;\n\t@q mbarrier.arrive.shared::cta.b64 _, [%0];\n\t}" ::"r"(
+          smem_u32(bar)),
+      "r"(issue)
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx_if(uint32_t issue, uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t"
+      "@q mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+      "r"(bytes), "r"(issue)
+      : "memory");
+}
+
 // Adds `bytes` to the transaction count of the current phase (no arrival).
 __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
@@ -64,12 +80,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // raised *abort_flag, so one failed wait stops the whole CTA instead of
 // leaving its other warps spinning.  The fast path is a single try_wait; the
 // clock and the flag are only read while the wait is actually blocked.
+//
+// sleep_ns > 0 makes a blocked waiter back off with __nanosleep between polls,
+// so that warps with long waits (the epilogue) leave their scheduler's issue
+// slots to the producer and MMA warps that share it.
 __device__ __forceinline__ bool wait_parity(uint64_t* bar, uint32_t parity,
                                             volatile int* abort_flag, unsigned* err,
-                                            uint32_t tag, long long timeout_cycles) {
+                                            uint32_t tag, long long timeout_cycles,
+                                            unsigned sleep_ns = 0) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   for (uint32_t it = 1;; ++it) {
+    if (sleep_ns) __nanosleep(sleep_ns);
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 15u) == 0u) {
       if (*abort_flag) return false;
@@ -107,6 +129,30 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, in
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::"
       "cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Predicated forms: the instruction executes only where `issue` is nonzero.
+// Warp-uniform code calls these with issue = (lane == 0), so the issuing warp
+// never diverges around the single-thread instructions.
+__device__ __forceinline__ void tma_load_2d_if(uint32_t issue, void* smem_dst, const void* tmap, int32_t x,
+                                               int32_t y, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %6, 0;\n\t"
+      "@q cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::"
+      "cache_hint [%0], [%1, {%2, %3}], [%4], %5;\n\t}" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy), "r"(issue)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_if(uint32_t issue, void* smem_dst, const void* tmap, int32_t x,
+                                               int32_t y, int32_t z, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %7, 0;\n\t"
+      "@q cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::"
+      "cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;\n\t}" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy),
+      "r"(issue)
       : "memory");
 }
 
@@ -156,6 +202,46 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uin
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
       "}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_f16_ss_if(uint32_t issue, uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t"
+      ".reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.ne.b32 q, %5, 0;\n\t"
+      "@q tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t"
+      "}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(issue)
+      : "memory");
+}
+
+// Same, with the 64-bit descriptors passed as (low, high) 32-bit halves; the
+// start address lives in the low half, so callers advance a descriptor with
+// one 32-bit add.
+__device__ __forceinline__ void mma_f16_ss_if(uint32_t issue, uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi,
+                                              uint32_t b_lo, uint32_t b_hi, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t"
+      ".reg .pred p, q;\n\t"
+      ".reg .b64 ad, bd;\n\t"
+      "setp.ne.b32 p, %7, 0;\n\t"
+      "setp.ne.b32 q, %8, 0;\n\t"
+      "mov.b64 ad, {%1, %2};\n\t"
+      "mov.b64 bd, {%3, %4};\n\t"
+      "@q tcgen05.mma.cta_group::1.kind::f16 [%0], ad, bd, %5, p;\n\t"
+      "}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(0u), "r"(accumulate), "r"(issue)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit_if(uint32_t issue, uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %1, 0;\n\t"
+      "@q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(smem_u32(bar)),
+      "r"(issue)
       : "memory");
 }
 

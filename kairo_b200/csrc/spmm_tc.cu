@@ -80,8 +80,7 @@ struct TcArgs {
   int32_t row_cost;
   int32_t stages;          // stage groups in the shared-memory ring
   int32_t group;           // blocks per stage group
-  int32_t nacc;            // independent accumulators per row piece (1..4)
-  uint32_t tmem_cols;      // TMEM columns allocated (power of two, >= 2*nacc*NT*BM)
+  uint32_t tmem_cols;      // TMEM columns allocated (power of two, >= 2*NT*BM)
   int32_t vec_store;       // LINEAR: rows of Y may be written with 16-byte stores
   int32_t b_box3d;         // STANDARD: the whole B panel is one 3D box (N % 64 == 0)
 };
@@ -284,7 +283,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int PART_ELEMS = NT * BM * 128;
   static_assert(BK % 16 == 0 && BM % 16 == 0 && BM <= 256, "block shape");
   static_assert(2 * ACC_COLS <= 512, "TMEM budget");
-  const int NACC = args.nacc;                 // accumulators per TMEM slot
   const uint32_t TMEM_COLS = args.tmem_cols;
 
   extern __shared__ uint8_t smem_raw[];
@@ -349,9 +347,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Blocks are loaded in groups of GB consecutive blocks per stage: one
     // lane per block issues that block's two TMA loads, so a whole group is
     // issued by a couple of warp instructions, and the group's full barrier
-    // gets a single arrival once every block of it has its expect_tx.
+    // gets a single arrival once every block of it has its expect_tx.  The
+    // warp stays converged: waits are polled by all lanes and single-lane
+    // instructions are predicated, never branched around.
     const uint64_t pol_a = ptx::policy_evict_first();
     const uint64_t pol_b = ptx::policy_evict_last();
+    const uint32_t leader = lane == 0 ? 1u : 0u;
     int gpos = 0;      // next slot in the current group
     int gidx = 0;      // stage of the current group
     uint32_t gph = 0;  // phase of that stage
@@ -375,36 +376,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         while (j0 < cnt) {
           const int take = min(GB - gpos, cnt - j0);
           if (gpos == 0) {
-            int ok = 1;
-            if (lane == 0) {
-              ok = ptx::wait_parity(&empty[gidx], gph ^ 1u, abort_flag, args.err, kTagEmpty, kWaitCycles);
-              if (ok) issued[gidx] = static_cast<int>(gph) + 1;
-            }
+            int ok = ptx::wait_parity(&empty[gidx], gph ^ 1u, abort_flag, args.err, kTagEmpty, kWaitCycles);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) return false;
+            if (lane == 0) issued[gidx] = static_cast<int>(gph) + 1;
           }
-          if (lane >= j0 && lane < j0 + take) {
-            uint8_t* st = smem + (gidx * GB + gpos + (lane - j0)) * SLOT_BYTES;
-            ptx::mbar_expect_tx(&full[gidx], TX_BYTES);
-            ptx::tma_load_2d(st + PANEL_BYTES, &tmap_a, 0, mb * BM, &full[gidx], pol_a);
-            if (LINEAR) {
-              // X rows n0 .. n0+128*NT as one box: sub-tile t lands at t*128*BK*2.
-              ptx::tma_load_2d(st, &tmap_b, mc * BK, n0, &full[gidx], pol_b);
-            } else if (args.b_box3d) {
-              // B viewed as [N/64][K][64]: the 2*NT column atoms of the
-              // panel arrive as [atom][k][64] in one box.
-              ptx::tma_load_3d(st, &tmap_b, 0, mc * BK, n0 / 64, &full[gidx], pol_b);
-            } else {
+          const uint32_t mine = (lane >= j0 && lane < j0 + take) ? 1u : 0u;
+          uint8_t* st = smem + (gidx * GB + gpos + (lane - j0)) * SLOT_BYTES;
+          ptx::mbar_expect_tx_if(mine, &full[gidx], TX_BYTES);
+          ptx::tma_load_2d_if(mine, st + PANEL_BYTES, &tmap_a, 0, mb * BM, &full[gidx], pol_a);
+          if (LINEAR) {
+            // X rows n0 .. n0+128*NT as one box: sub-tile t lands at t*128*BK*2.
+            ptx::tma_load_2d_if(mine, st, &tmap_b, mc * BK, n0, &full[gidx], pol_b);
+          } else if (args.b_box3d) {
+            // B viewed as [N/64][K][64]: the 2*NT column atoms of the
+            // panel arrive as [atom][k][64] in one box.
+            ptx::tma_load_3d_if(mine, st, &tmap_b, 0, mc * BK, n0 / 64, &full[gidx], pol_b);
+          } else {
 #pragma unroll
-              for (int h = 0; h < 2 * NT; ++h)
-                ptx::tma_load_2d(st + h * BK * 128, &tmap_b, n0 + 64 * h, mc * BK, &full[gidx], pol_b);
-            }
+            for (int h = 0; h < 2 * NT; ++h)
+              ptx::tma_load_2d_if(mine, st + h * BK * 128, &tmap_b, n0 + 64 * h, mc * BK, &full[gidx], pol_b);
           }
           __syncwarp();
           gpos += take;
           j0 += take;
           if (gpos == GB) {
-            if (lane == 0) ptx::mbar_arrive(&full[gidx]);
+            ptx::mbar_arrive_if(leader, &full[gidx]);
             gpos = 0;
             if (++gidx == S) {
               gidx = 0;
@@ -417,12 +414,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     });
     // Close a partly filled last group (also after an abort, so that the
     // loads already issued can complete its phase before the drain below).
-    if (gpos != 0 && lane == 0) ptx::mbar_arrive(&full[gidx]);
+    if (gpos != 0) ptx::mbar_arrive_if(leader, &full[gidx]);
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    // Lane 0 issues every MMA.  Descriptors are built once and advanced by
-    // adding (byte offset >> 4) to their start-address field.
+    // The whole warp runs the loop (uniform control flow); lane 0 is the
+    // only one whose MMA / commit instructions are enabled.  Descriptors are
+    // built once and advanced by adding (byte offset >> 4) to their
+    // start-address field.
+    const uint32_t leader = lane == 0 ? 1u : 0u;
     int mpos = 0, midx = 0;
     uint32_t mph = 0;
     int slot = 0;
@@ -431,63 +431,63 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint64_t adesc0 = LINEAR ? ptx::make_smem_desc(sbase, 16, 8 * BK * 2, SW_ROW)
                                    : ptx::make_smem_desc(sbase, BK * 128, 1024, 2u);
     const uint64_t bdesc0 = ptx::make_smem_desc(sbase + PANEL_BYTES, 16, 8 * BK * 2, SW_ROW);
+    const uint32_t a_lo0 = static_cast<uint32_t>(adesc0), a_hi = static_cast<uint32_t>(adesc0 >> 32);
+    const uint32_t b_lo0 = static_cast<uint32_t>(bdesc0), b_hi = static_cast<uint32_t>(bdesc0 >> 32);
+    constexpr uint32_t SLOT16 = SLOT_BYTES >> 4;
+    uint32_t slot16 = 0;  // (byte offset of the current block slot) >> 4
     walk_items(args, s_range, e_range, i_start, lane, [&](const RowItem& it) -> bool {
       if (it.kind != kDirect && it.kind != kPartial) return true;
-      int ok = 1;
-      if (lane == 0) {
-        ok = ptx::wait_parity(&tempty[slot], aphase ^ 1u, abort_flag, args.err, kTagTmemEmpty, kWaitCycles);
-        if (ok) {
-          ptx::tc_fence_after();
-          // Consecutive blocks of a row piece go to NACC independent
-          // accumulators, so back-to-back MMAs do not wait on each other's
-          // accumulator update; the epilogue adds the NACC partial sums.
-          const uint32_t slot_base = tmem_base + static_cast<uint32_t>(slot * NACC * ACC_COLS);
-          int acc = 0;
-          for (int p = it.p0; p < it.p1; ++p) {
-            const uint32_t d_base = slot_base + static_cast<uint32_t>(acc * ACC_COLS);
-            const bool first = (p - it.p0) < NACC;
-            if (mpos == 0) {
-              ok = ptx::wait_parity(&full[midx], mph, abort_flag, args.err, kTagFull, kWaitCycles);
-              if (!ok) break;
-              ptx::tc_fence_after();
-            }
-            const uint64_t off16 = static_cast<uint64_t>(((midx * GB + mpos) * SLOT_BYTES) >> 4);
-#pragma unroll
-            for (int kk = 0; kk < BK / 16; ++kk) {
-              const uint64_t bdesc = bdesc0 + off16 + static_cast<uint64_t>((kk * 32) >> 4);
-#pragma unroll
-              for (int t = 0; t < NT; ++t) {
-                const uint32_t a_off = LINEAR ? (t * 128 * BK * 2 + kk * 32) : (t * 2 * BK * 128 + kk * 2048);
-                ptx::mma_f16_ss(d_base + t * BM, adesc0 + off16 + (a_off >> 4), bdesc, IDESC,
-                                (!first || kk > 0) ? 1u : 0u);
-              }
-            }
-            if (++acc == NACC) acc = 0;
-            if (++mpos == GB) {
-              ptx::mma_commit(&empty[midx]);
-              mpos = 0;
-              if (++midx == S) {
-                midx = 0;
-                mph ^= 1u;
-              }
-            }
-          }
-          if (ok) ptx::mma_commit(&tfull[slot]);
-        }
-      }
+      int ok = ptx::wait_parity(&tempty[slot], aphase ^ 1u, abort_flag, args.err, kTagTmemEmpty, kWaitCycles);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) return false;
+      ptx::tc_fence_after();
+      const uint32_t d_base = tmem_base + static_cast<uint32_t>(slot * ACC_COLS);
+      int p = it.p0;
+      while (p < it.p1) {
+        if (mpos == 0) {
+          ok = ptx::wait_parity(&full[midx], mph, abort_flag, args.err, kTagFull, kWaitCycles);
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) return false;
+          ptx::tc_fence_after();
+          slot16 = static_cast<uint32_t>(midx * GB) * SLOT16;
+        }
+        // Blocks [p, p + seg) all live in the current stage group.
+        const int seg = min(it.p1 - p, GB - mpos);
+        const int p_end = p + seg;
+#pragma unroll 2
+        for (; p < p_end; ++p) {
+          const uint32_t acc_any = (p != it.p0) ? 1u : 0u;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+#pragma unroll
+            for (int t = 0; t < NT; ++t) {
+              const uint32_t a_off = LINEAR ? (t * 128 * BK * 2 + kk * 32) : (t * 2 * BK * 128 + kk * 2048);
+              ptx::mma_f16_ss_if(leader, d_base + t * BM, a_lo0 + slot16 + (a_off >> 4), a_hi,
+                                 b_lo0 + slot16 + ((kk * 32) >> 4), b_hi, IDESC, (acc_any | (kk > 0)) ? 1u : 0u);
+            }
+          }
+          slot16 += SLOT16;
+        }
+        mpos += seg;
+        if (mpos == GB) {
+          ptx::mma_commit_if(leader, &empty[midx]);
+          mpos = 0;
+          if (++midx == S) {
+            midx = 0;
+            mph ^= 1u;
+          }
+        }
+      }
+      ptx::mma_commit_if(leader, &tfull[slot]);
       slot ^= 1;
       if (slot == 0) aphase ^= 1u;
       return true;
     });
     // Every MMA issued above has completed once mma_done flips.
-    if (lane == 0) {
-      if (mpos != 0) ptx::mma_commit(&empty[midx]);
-      ptx::mma_commit(mma_done);
-      int dummy = 0;
-      ptx::wait_parity(mma_done, 0, reinterpret_cast<volatile int*>(&dummy), args.err, kTagDrain, kWaitCycles);
-    }
+    if (mpos != 0) ptx::mma_commit_if(leader, &empty[midx]);
+    ptx::mma_commit_if(leader, mma_done);
+    int dummy = 0;
+    ptx::wait_parity(mma_done, 0, reinterpret_cast<volatile int*>(&dummy), args.err, kTagDrain, kWaitCycles);
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
@@ -508,40 +508,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j0 = 0; j0 < BM; j0 += 16) store16<LINEAR, TOut>(args, it.row, BM, j0, n0 + t * 128 + e, z);
         return true;
       }
-      int ok = 1;
-      if (lane == 0)
-        ok = ptx::wait_parity(&tfull[slot], aphase, abort_flag, args.err, kTagTmemFull, kWaitCycles);
+      int ok = ptx::wait_parity(&tfull[slot], aphase, abort_flag, args.err, kTagTmemFull, kWaitCycles, 200);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (epi_any(!ok)) return false;
       ptx::tc_fence_after();
       float* part = nullptr;
       if (it.kind == kPartial)
         part = args.partials + (static_cast<int64_t>(it.group * G + blockIdx.x) * 2 + it.slot) * PART_ELEMS;
-      const int nsum = min(NACC, it.p1 - it.p0);  // accumulators this piece wrote
-      const uint32_t slot_cols = static_cast<uint32_t>(slot * NACC * ACC_COLS);
+      const uint32_t slot_cols = static_cast<uint32_t>(slot * ACC_COLS);
 #pragma unroll
       for (int t = 0; t < NT; ++t) {
 #pragma unroll
         for (int j0 = 0; j0 < BM; j0 += 16) {
-          float v[16], w1[16], w2[16], w3[16];
-          const uint32_t col = tmem_base + lane_addr + slot_cols + static_cast<uint32_t>(t * BM + j0);
-          ptx::tmem_ld16(col, v);
-          if (nsum > 1) ptx::tmem_ld16(col + ACC_COLS, w1);
-          if (nsum > 2) ptx::tmem_ld16(col + 2 * ACC_COLS, w2);
-          if (nsum > 3) ptx::tmem_ld16(col + 3 * ACC_COLS, w3);
+          float v[16];
+          ptx::tmem_ld16(tmem_base + lane_addr + slot_cols + static_cast<uint32_t>(t * BM + j0), v);
           ptx::tmem_wait_ld();
-          if (nsum > 1) {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) v[jj] += w1[jj];
-          }
-          if (nsum > 2) {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) v[jj] += w2[jj];
-          }
-          if (nsum > 3) {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) v[jj] += w3[jj];
-          }
           if (it.kind == kDirect) {
             store16<LINEAR, TOut>(args, it.row, BM, j0, n0 + t * 128 + e, v);
           } else {
@@ -807,12 +788,8 @@ kairo_status tc_plan(const kairo_bsr* a, int32_t layout, int64_t n, const kairo_
   if (stages < 2) return fail(KAIRO_STATUS_NOT_SUPPORTED, "shared memory too small for two pipeline stages");
   p.group = group;
   p.stages = stages;
-  // Up to four accumulators per TMEM slot, two slots, within 512 columns.
-  int nacc = 512 / (2 * nt * p.bm);
-  if (nacc > 4) nacc = 4;
-  if (nacc < 1) nacc = 1;
-  p.nacc = nacc;
-  const int need = 2 * nacc * nt * p.bm;
+  // Two accumulator slots (double buffering between MMA and epilogue).
+  const int need = 2 * nt * p.bm;
   p.tmem_cols = 32;
   while (p.tmem_cols < static_cast<uint32_t>(need)) p.tmem_cols <<= 1;
   p.smem_bytes = static_cast<size_t>(stages) * group * sb + reserve;
@@ -878,7 +855,6 @@ kairo_status tc_launch(const kairo_bsr* a, const void* b, int64_t ldb, int32_t l
   args.row_cost = plan.row_cost;
   args.stages = plan.stages;
   args.group = plan.group;
-  args.nacc = plan.nacc;
   args.tmem_cols = plan.tmem_cols;
   const size_t osz = elem_size(c_dtype);
   args.b_box3d = b_box3d;

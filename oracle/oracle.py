@@ -82,6 +82,8 @@ def spmm_tiles(tiles: torch.Tensor, row_ids: torch.Tensor, col_ids: torch.Tensor
     B = _cpu(B)
     r = _cpu(row_ids, torch.int32)
     c = _cpu(col_ids, torch.int32)
+    if B.dim() != 2 or B.shape[0] < K or B.shape[1] < N:
+        raise ValueError(f"B must be at least ({K}, {N}), got {tuple(B.shape)}")
     C = torch.empty(M, N, dtype=torch.float32)
     rc = load().oracle_spmm_tiles(tiles.data_ptr(), _DT[tiles.dtype], r.data_ptr(), c.data_ptr(), r.numel(),
                                   B.data_ptr(), _DT[B.dtype], M, K, N, tile_m, tile_k, C.data_ptr(), nthreads)
@@ -99,7 +101,11 @@ def spmm_bsr_rows(row_ptr: torch.Tensor, col_idx: torch.Tensor, blk_idx: torch.T
     blocks = _cpu(blocks)
     B = _cpu(B)
     bm, bk = int(blocks.shape[1]), int(blocks.shape[2])
+    if B.dim() != 2 or B.shape[0] < K or B.shape[1] < N:
+        raise ValueError(f"B must be at least ({K}, {N}), got {tuple(B.shape)}")
     sel = torch.as_tensor(rows_sel, dtype=torch.int32).contiguous()
+    if sel.numel() and (int(sel.min()) < 0 or int(sel.max()) >= rp.numel() - 1):
+        raise ValueError("selected block-row out of range")
     out = torch.empty(sel.numel() * bm, N, dtype=torch.float32)
     rc = load().oracle_spmm_bsr_rows(rp.data_ptr(), ci.data_ptr(), None if bi is None else bi.data_ptr(),
                                      blocks.data_ptr(), _DT[blocks.dtype], bm, bk, B.data_ptr(), _DT[B.dtype],
