@@ -80,7 +80,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "50", *self.sel], stdout=subprocess.PIPE,
+                                          "-lms", "10", *self.sel], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -275,18 +275,19 @@ def run_ours(args) -> None:
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
-    for _ in range(args.warmup):
-        flush.zero_()
-        step()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    # Clock samples are taken from the last warm-up steps through the timed
+    # region (every 10 ms), so that short timed regions still get samples.
     sampler = ClockSampler(dev)
     with sampler:
+        for _ in range(args.warmup):
+            flush.zero_()
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         wall0 = time.perf_counter()
         for i in range(args.steps):
             flush.zero_()
