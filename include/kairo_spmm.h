@@ -124,6 +124,21 @@ KAIRO_API kairo_status kairo_bsr_spmm(const kairo_bsr* a, const void* b, int64_t
                             kairo_dtype c_dtype, const kairo_spmm_config* cfg,
                             void* workspace, size_t workspace_bytes, void* stream);
 
+/* kairo_bsr_spmm without a workspace argument, for callers that cannot
+ * allocate device memory (a framework that forbids plugins to cudaMalloc, a
+ * path that must not stall the device, a stateless callback).  This entry
+ * point has no counterpart in the reference.  Its scratch is a 32 MiB array
+ * built into the library, one per device: every GPU that loads the library
+ * holds it until the process exits.  Problems needing more scratch than that
+ * return KAIRO_STATUS_NOT_SUPPORTED.  The first call on a device looks up the
+ * array's device address (make it before any stream capture).  Each call
+ * clears the array's error word and counters on `stream`.  Calls share the
+ * array, so calls whose launches overlap on the GPU race: order them. */
+KAIRO_API kairo_status kairo_bsr_spmm_noalloc(const kairo_bsr* a, const void* b, int64_t ldb,
+                                              int32_t layout, int64_t n, void* c, int64_t ldc,
+                                              kairo_dtype c_dtype, const kairo_spmm_config* cfg,
+                                              void* stream);
+
 /* Bytes of zero-initialised workspace kairo_bsr_spmm needs for this problem. */
 KAIRO_API kairo_status kairo_bsr_spmm_workspace_size(const kairo_bsr* a, int32_t layout, int64_t n,
                                            const kairo_spmm_config* cfg, size_t* bytes);

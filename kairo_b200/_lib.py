@@ -111,6 +111,8 @@ _lib_lock = threading.Lock()
 _SIGNATURES = {
     "kairo_bsr_spmm": (c_int32, [POINTER(KairoBsr), c_void_p, c_int64, c_int32, c_int64, c_void_p, c_int64,
                                  c_int32, POINTER(KairoSpmmConfig), c_void_p, c_size_t, c_void_p]),
+    "kairo_bsr_spmm_noalloc": (c_int32, [POINTER(KairoBsr), c_void_p, c_int64, c_int32, c_int64, c_void_p,
+                                         c_int64, c_int32, POINTER(KairoSpmmConfig), c_void_p]),
     "kairo_bsr_spmm_workspace_size": (c_int32, [POINTER(KairoBsr), c_int32, c_int64, POINTER(KairoSpmmConfig),
                                                 POINTER(c_size_t)]),
     "kairo_bsr_build": (c_int32, [c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p, c_void_p, c_void_p,
