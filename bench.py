@@ -233,7 +233,7 @@ def run_reference(args) -> None:
 def run_ours(args) -> None:
     import torch.distributed as dist
 
-    from kairo_b200.ops import KernelConfig, block_sparse_mm_bsr, bsr_from_tiles
+    from kairo_b200.ops import KernelConfig, block_sparse_mm_bsr, bsr_from_tiles, describe
     from kairo_b200.sharding import gather_rows, partition_rows, shard_bsr
 
     rank, world, local = dist_env()
@@ -254,8 +254,10 @@ def run_ours(args) -> None:
     local_nnzb = a.nnzb
     local_rows = a.shape[0]
     b = problem.b
-    cfg = KernelConfig(n_tile=args.n_tile, group_blocks=args.group_blocks)
+    cfg = KernelConfig(n_tile=args.n_tile, group_blocks=args.group_blocks, schedule=args.schedule,
+                       band_rows=args.band_rows)
     linear = spec.layout == "linear"
+    plan = describe(a, spec.n, linear=linear, config=cfg)
     out_rows = local_rows
     if linear:
         from kairo_b200.ops import sparse_linear
@@ -370,7 +372,10 @@ def run_ours(args) -> None:
                 "sparsity": spec.sparsity, "nnzb": a_full.nnzb, "out_dtype": str(spec.out_dtype).replace("torch.", ""),
                 "parallelism": f"row-shard{world} (nnz-balanced block rows, B replicated)",
                 "l2": "flushed before every step (256 MiB write, untimed)",
-                "kernel_config": {"n_tile": args.n_tile, "group_blocks": args.group_blocks},
+                "kernel_config": {"n_tile": args.n_tile, "group_blocks": args.group_blocks,
+                                  "schedule": args.schedule, "band_rows": args.band_rows,
+                                  "max_row_blocks": a.max_row_blocks},
+                "plan": plan,
             },
             "roofline": {
                 "bound": "hbm",
@@ -386,7 +391,7 @@ def run_ours(args) -> None:
             },
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * plan["launches"],
             "clocks": clocks,
             "wall_s_timed_region": wall,
         }
@@ -420,7 +425,8 @@ def run_e2e(args, spec, a, b, out, cfg, dev, stream, linear, world, dist):
         d_rp.copy_(h_rp, non_blocking=True)
         d_ci.copy_(h_ci, non_blocking=True)
         d_b.copy_(h_b, non_blocking=True)
-        m = BlockSparseMatrix(row_ptr=d_rp, col_idx=d_ci, blocks=d_blocks, shape=a.shape, block_size=a.block_size)
+        m = BlockSparseMatrix(row_ptr=d_rp, col_idx=d_ci, blocks=d_blocks, shape=a.shape, block_size=a.block_size,
+                              max_row_blocks=a.max_row_blocks)
         if linear:
             sparse_linear(d_b, m, out=out, config=cfg)
         else:
@@ -465,6 +471,8 @@ def main() -> None:
                     "for profiling smaller cases")
     ap.add_argument("--n-tile", type=int, default=0)
     ap.add_argument("--group-blocks", type=int, default=0)
+    ap.add_argument("--schedule", choices=("auto", "rows", "bands"), default="auto")
+    ap.add_argument("--band-rows", type=int, default=0)
     ap.add_argument("--gather", action="store_true", help="also time the all-gather of C (reported separately)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)

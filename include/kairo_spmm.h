@@ -40,7 +40,7 @@
 extern "C" {
 #endif
 
-#define KAIRO_ABI_VERSION 1
+#define KAIRO_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define KAIRO_API __attribute__((visibility("default")))
@@ -91,7 +91,7 @@ typedef struct kairo_bsr {
   const int32_t* blk_idx;    /* nnzb, or NULL for identity */
   const void* blocks;        /* (nblocks_stored, bm, bk) row-major, dtype below */
   kairo_dtype dtype;
-  int32_t reserved1;
+  int32_t max_row_blocks;    /* longest block-row in blocks, if known (0 = unknown); informational */
 } kairo_bsr;
 
 /* Tuning knobs of one launch; zero-initialised means "library default". */
@@ -102,8 +102,24 @@ typedef struct kairo_spmm_config {
   int32_t row_cost;          /* scheduler weight of one block-row in units of one block (0 = auto) */
   int32_t num_ctas;          /* persistent grid size (0 = one CTA per SM) */
   int32_t group_blocks;      /* nonzero blocks per pipeline stage, 1..32 (0 = auto) */
-  int32_t reserved[2];
+  int32_t schedule;          /* kairo_schedule (tcgen05 kernel only) */
+  int32_t band_rows;         /* block-rows per item of the band schedule (0 = auto) */
+  int32_t reserved[4];
 } kairo_spmm_config;
+
+/* Work schedules of the tcgen05 kernel.
+ * ROWS:  block-rows split over CTAs by a merge path over (rows, blocks); long
+ *        rows are cut and their pieces summed in a fixed order.  Robust to
+ *        skewed masks.
+ * BANDS: each CTA holds `band_rows` block-rows in TMEM and visits their
+ *        blocks in column order, all CTAs sweeping B together so gathered B
+ *        panels are shared through L2.  Rows are never cut.
+ * AUTO picks ROWS. */
+typedef enum kairo_schedule {
+  KAIRO_SCHEDULE_AUTO = 0,
+  KAIRO_SCHEDULE_ROWS = 1,
+  KAIRO_SCHEDULE_BANDS = 2
+} kairo_schedule;
 
 /* Operand layouts of kairo_bsr_spmm. */
 #define KAIRO_LAYOUT_STANDARD 0  /* B is (K x N), C is (M x N):  C = A * B            */
@@ -139,6 +155,24 @@ KAIRO_API kairo_status kairo_bsr_spmm_noalloc(const kairo_bsr* a, const void* b,
                                               kairo_dtype c_dtype, const kairo_spmm_config* cfg,
                                               void* stream);
 
+/* What kairo_bsr_spmm would run for this problem (no device work).  Fills
+ * `out` from the same decision as kairo_bsr_spmm_workspace_size, assuming
+ * 16-byte aligned operands.  No counterpart in the reference; used by the
+ * autotuner and benchmarks to report the kernel and its launch count. */
+typedef struct kairo_spmm_plan {
+  int32_t kernel;            /* kairo_kernel actually used (0 = nothing to compute) */
+  int32_t schedule;          /* kairo_schedule used by the tcgen05 kernel (0 otherwise) */
+  int32_t launches;          /* kernel launches per call */
+  int32_t grid;              /* CTAs of the main kernel */
+  int32_t n_tile;            /* C columns per work item */
+  int32_t stages;            /* pipeline stages */
+  int32_t group_blocks;      /* blocks per stage */
+  int32_t rows;              /* band_rows (BANDS) or row_cost (ROWS) */
+  uint64_t workspace_bytes;
+} kairo_spmm_plan;
+KAIRO_API kairo_status kairo_bsr_spmm_describe(const kairo_bsr* a, int32_t layout, int64_t n,
+                                               const kairo_spmm_config* cfg, kairo_spmm_plan* out);
+
 /* Bytes of zero-initialised workspace kairo_bsr_spmm needs for this problem. */
 KAIRO_API kairo_status kairo_bsr_spmm_workspace_size(const kairo_bsr* a, int32_t layout, int64_t n,
                                            const kairo_spmm_config* cfg, size_t* bytes);
@@ -150,7 +184,9 @@ KAIRO_API kairo_status kairo_bsr_spmm_workspace_size(const kairo_bsr* a, int32_t
  * (sparse_embedding.py:23-46, here int32).  `perm` receives the stored-block
  * index of every BSR position (use it as kairo_bsr.blk_idx).  *is_identity
  * (host) tells whether the input was already row-sorted (perm[p] == p); when
- * it is, callers may pass blk_idx = NULL.  Ids outside [0, nbr) x [0, nbc)
+ * it is, callers may pass blk_idx = NULL.  *max_row_blocks (host, may be
+ * NULL) receives the longest block-row, for kairo_bsr.max_row_blocks.
+ * Ids outside [0, nbr) x [0, nbc)
  * raise INVALID_VALUE.  Unsorted input is supported when no block-row holds
  * more than 16384 tiles (NOT_SUPPORTED otherwise).
  * This call synchronises `stream` once (it reads two flags back).
@@ -158,8 +194,8 @@ KAIRO_API kairo_status kairo_bsr_spmm_workspace_size(const kairo_bsr* a, int32_t
 KAIRO_API kairo_status kairo_bsr_build(const int32_t* tile_row_ids, const int32_t* tile_col_ids,
                              int64_t num_tiles, int32_t nbr, int32_t nbc,
                              int32_t* row_ptr, int32_t* col_idx, int32_t* perm,
-                             int32_t* is_identity, void* workspace, size_t workspace_bytes,
-                             void* stream);
+                             int32_t* is_identity, int32_t* max_row_blocks, void* workspace,
+                             size_t workspace_bytes, void* stream);
 KAIRO_API kairo_status kairo_bsr_build_workspace_size(int64_t num_tiles, int32_t nbr, size_t* bytes);
 
 /* ------------------------------------------------------------------------

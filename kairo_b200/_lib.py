@@ -40,6 +40,13 @@ KERNEL_TCGEN05 = 2
 LAYOUT_STANDARD = 0
 LAYOUT_LINEAR = 1
 
+# kairo_schedule
+SCHEDULE_AUTO = 0
+SCHEDULE_ROWS = 1
+SCHEDULE_BANDS = 2
+
+ABI_VERSION = 2
+
 # device error codes (low 8 bits of the workspace error word)
 DEVERR_NONE = 0
 DEVERR_WAIT_TIMEOUT = 1
@@ -64,7 +71,7 @@ class KairoBsr(Structure):
         ("blk_idx", c_void_p),
         ("blocks", c_void_p),
         ("dtype", c_int32),
-        ("reserved1", c_int32),
+        ("max_row_blocks", c_int32),
     ]
 
 
@@ -76,7 +83,23 @@ class KairoSpmmConfig(Structure):
         ("row_cost", c_int32),
         ("num_ctas", c_int32),
         ("group_blocks", c_int32),
-        ("reserved", c_int32 * 2),
+        ("schedule", c_int32),
+        ("band_rows", c_int32),
+        ("reserved", c_int32 * 4),
+    ]
+
+
+class KairoSpmmPlan(Structure):
+    _fields_ = [
+        ("kernel", c_int32),
+        ("schedule", c_int32),
+        ("launches", c_int32),
+        ("grid", c_int32),
+        ("n_tile", c_int32),
+        ("stages", c_int32),
+        ("group_blocks", c_int32),
+        ("rows", c_int32),
+        ("workspace_bytes", ctypes.c_uint64),
     ]
 
 
@@ -113,10 +136,12 @@ _SIGNATURES = {
                                  c_int32, POINTER(KairoSpmmConfig), c_void_p, c_size_t, c_void_p]),
     "kairo_bsr_spmm_noalloc": (c_int32, [POINTER(KairoBsr), c_void_p, c_int64, c_int32, c_int64, c_void_p,
                                          c_int64, c_int32, POINTER(KairoSpmmConfig), c_void_p]),
+    "kairo_bsr_spmm_describe": (c_int32, [POINTER(KairoBsr), c_int32, c_int64, POINTER(KairoSpmmConfig),
+                                          POINTER(KairoSpmmPlan)]),
     "kairo_bsr_spmm_workspace_size": (c_int32, [POINTER(KairoBsr), c_int32, c_int64, POINTER(KairoSpmmConfig),
                                                 POINTER(c_size_t)]),
     "kairo_bsr_build": (c_int32, [c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p, c_void_p, c_void_p,
-                                  POINTER(c_int32), c_void_p, c_size_t, c_void_p]),
+                                  POINTER(c_int32), POINTER(c_int32), c_void_p, c_size_t, c_void_p]),
     "kairo_bsr_build_workspace_size": (c_int32, [c_int64, c_int32, POINTER(c_size_t)]),
     "kairo_dense_to_tiles": (c_int32, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int32,
                                        c_int32, c_void_p, c_void_p]),
@@ -155,7 +180,7 @@ def lib() -> ctypes.CDLL:
             fn = getattr(handle, name)
             fn.restype = restype
             fn.argtypes = argtypes
-        if handle.kairo_abi_version() != 1:
+        if handle.kairo_abi_version() != ABI_VERSION:
             raise KairoLibraryError("libkairo_spmm ABI version mismatch")
         _lib = handle
         return handle

@@ -227,7 +227,8 @@ extern "C" kairo_status kairo_bsr_build_workspace_size(int64_t num_tiles, int32_
 
 extern "C" kairo_status kairo_bsr_build(const int32_t* tile_row_ids, const int32_t* tile_col_ids, int64_t num_tiles,
                                         int32_t nbr, int32_t nbc, int32_t* row_ptr, int32_t* col_idx, int32_t* perm,
-                                        int32_t* is_identity, void* workspace, size_t workspace_bytes, void* stream) {
+                                        int32_t* is_identity, int32_t* max_row_blocks, void* workspace,
+                                        size_t workspace_bytes, void* stream) {
   if (num_tiles < 0 || nbr < 0 || nbc < 0) return fail(KAIRO_STATUS_INVALID_VALUE, "negative size");
   if (num_tiles > 0x7fffffffLL) return fail(KAIRO_STATUS_NOT_SUPPORTED, "more than 2^31-1 tiles");
   if (!row_ptr || !workspace || (num_tiles > 0 && (!tile_row_ids || !tile_col_ids || !col_idx || !perm)))
@@ -270,6 +271,7 @@ extern "C" kairo_status kairo_bsr_build(const int32_t* tile_row_ids, const int32
     return fail(KAIRO_STATUS_NOT_SUPPORTED, "unsorted tile list with a block-row longer than 16384 tiles");
   if (code) return fail(KAIRO_STATUS_DEVICE_ERROR, "device error during BSR build");
   if (is_identity) *is_identity = (reinterpret_cast<int*>(hdr)[16] == 0) ? 1 : 0;
+  if (max_row_blocks) *max_row_blocks = reinterpret_cast<int*>(hdr)[17];
   return KAIRO_STATUS_SUCCESS;
 }
 

@@ -5,6 +5,7 @@
 #include <cstdint>
 #include <string>
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "../../include/kairo_spmm.h"
@@ -32,6 +33,28 @@ constexpr size_t kWorkspaceHeaderBytes = 256;  // error word + reserved
 constexpr int kCounterBankEntries = 16384;
 constexpr size_t kCounterRegionBytes = 2 * kCounterBankEntries * sizeof(unsigned);
 
+// Blocks per pipeline stage when the caller leaves it to the library.  On
+// B200, TMA gathers of B panels into shared memory run faster in fewer,
+// larger stage groups while their data is in L2 (16 KB panels: 40, 49, 55 and
+// 60 B/clk per SM with groups of 2, 3, 4 and 6 blocks), whereas gathers that
+// miss L2 are bound by HBM and gain from more stages in flight instead.  So:
+// four stages when the B slice of one chunk exceeds half of L2; otherwise
+// three stages of the largest group that fits, or two when fewer than nine
+// block slots fit.
+inline int default_group_blocks(int slots, bool b_slice_exceeds_half_l2) {
+  const int stages = b_slice_exceeds_half_l2 ? 4 : (slots >= 9 ? 3 : 2);
+  int g = slots / stages;
+  if (g > 32) g = 32;
+  if (g < 1) g = 1;
+  return g;
+}
+
+// Bytes of the B (or X) columns one chunk of 128 * nt output columns reads.
+inline double b_slice_bytes(const kairo_bsr* a, int nt) { return static_cast<double>(a->cols) * 128.0 * nt * 2.0; }
+
+// L2 size of `device` in bytes (126 MB if the query fails).
+int device_l2_bytes(int device);
+
 // Scheduling plan of one tcgen05 launch (host side).
 struct TcPlan {
   int bm, bk, nt;          // block size, 128-column sub-tiles per work item
@@ -49,6 +72,46 @@ struct TcPlan {
   size_t partials_offset, partials_bytes;
   size_t workspace_bytes;
 };
+
+// TMA tensor maps (tma_maps.cu).  make_operand_maps builds the block-storage
+// map and the B map (3D MN-major panel view when N % 64 == 0, else 2D) or,
+// for the LINEAR layout, the X map; *b_box3d tells which B map was built.
+kairo_status make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
+                         uint64_t inner, uint64_t outer, uint64_t row_stride_elems, uint32_t box_inner,
+                         uint32_t box_outer, const char* what);
+kairo_status make_map_b3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t n, uint64_t k,
+                          uint64_t ldb, uint32_t bk, uint32_t atoms);
+kairo_status make_operand_maps(const kairo_bsr* a, const void* b, int64_t ldb, bool linear, int64_t n, int nt,
+                               CUtensorMap* map_a, CUtensorMap* map_b, int* b_box3d);
+
+// Scheduling plan of one band-schedule launch (host side).  An item is
+// (chunk of 128*nt columns of C, group of `rows` consecutive block-rows); its
+// blocks are visited in column order (a per-launch sort into `order`) so
+// that all CTAs sweep the B panels of a chunk together.
+struct BandPlan {
+  int bm, bk, nt;
+  int nchunks;
+  int rows;                // block-rows per item (R)
+  int row_groups;          // ceil(nbr / R)
+  int64_t nitems;          // nchunks * row_groups
+  int acc_slots;           // TMEM accumulator sets (2 = epilogue overlaps the next item)
+  int grid;
+  int stages;
+  int group;
+  int serpentine;          // odd item waves visit their blocks in descending column order
+  uint32_t tmem_cols;
+  size_t smem_bytes;
+  size_t order_offset, order_bytes;
+  size_t workspace_bytes;
+};
+
+// Band schedule (spmm_band.cu)
+bool band_supported(const kairo_bsr* a, std::string* why);
+kairo_status band_plan(const kairo_bsr* a, int32_t layout, int64_t n, const kairo_spmm_config* cfg,
+                       int device, BandPlan* plan);
+kairo_status band_launch(const kairo_bsr* a, const void* b, int64_t ldb, int32_t layout, int64_t n,
+                         void* c, int64_t ldc, kairo_dtype c_dtype, const BandPlan& plan,
+                         void* workspace, cudaStream_t stream);
 
 // tcgen05 path (spmm_tc.cu)
 bool tc_supported(const kairo_bsr* a, int32_t layout, int64_t n, int64_t ldb, int64_t ldc,

@@ -50,6 +50,19 @@ int device_sm_count(int device) {
   return cache[device];
 }
 
+int device_l2_bytes(int device) {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  if (device < 0 || device >= 64) return 126 << 20;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[device] == 0) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrL2CacheSize, device) != cudaSuccess || v <= 0) v = 126 << 20;
+    cache[device] = v;
+  }
+  return cache[device];
+}
+
 namespace {
 
 kairo_status validate_bsr(const kairo_bsr* a) {
@@ -68,11 +81,12 @@ kairo_status validate_bsr(const kairo_bsr* a) {
   return KAIRO_STATUS_SUCCESS;
 }
 
-enum class Path { kNone, kZero, kSimt, kTc };
+enum class Path { kNone, kZero, kSimt, kTc, kBand };
 
 struct Choice {
   Path path = Path::kNone;
   TcPlan plan{};
+  BandPlan band{};
 };
 
 kairo_status choose(const kairo_bsr* a, const void* b, int64_t ldb, int32_t layout, int64_t n, const void* c,
@@ -104,10 +118,24 @@ kairo_status choose(const kairo_bsr* a, const void* b, int64_t ldb, int32_t layo
   std::string why_tc, why_simt;
   const bool tc_ok = tc_supported(a, layout, n, ldb, ldc, c_dtype, b, c, &why_tc);
   const bool simt_ok = simt_supported(a, layout, c_dtype, &why_simt);
+  const int schedule = cfg ? cfg->schedule : KAIRO_SCHEDULE_AUTO;
+  if (schedule != KAIRO_SCHEDULE_AUTO && schedule != KAIRO_SCHEDULE_ROWS && schedule != KAIRO_SCHEDULE_BANDS)
+    return fail(KAIRO_STATUS_INVALID_VALUE, "unknown schedule selector");
+  if (schedule == KAIRO_SCHEDULE_BANDS && kernel == KAIRO_KERNEL_SIMT)
+    return fail(KAIRO_STATUS_INVALID_VALUE, "the band schedule runs on the tcgen05 kernel only");
   if (kernel == KAIRO_KERNEL_TCGEN05 || (kernel == KAIRO_KERNEL_AUTO && tc_ok)) {
     if (!tc_ok) return fail(KAIRO_STATUS_NOT_SUPPORTED, why_tc);
-    ch.path = Path::kTc;
-    st = tc_plan(a, layout, n, cfg, current_device(), &ch.plan);
+    const int dev = current_device();
+    std::string why_band;
+    if (schedule == KAIRO_SCHEDULE_BANDS && !band_supported(a, &why_band))
+      return fail(KAIRO_STATUS_NOT_SUPPORTED, why_band);
+    if (schedule == KAIRO_SCHEDULE_BANDS) {
+      ch.path = Path::kBand;
+      st = band_plan(a, layout, n, cfg, dev, &ch.band);
+    } else {
+      ch.path = Path::kTc;
+      st = tc_plan(a, layout, n, cfg, dev, &ch.plan);
+    }
     if (st) return st;
   } else if (kernel == KAIRO_KERNEL_SIMT || kernel == KAIRO_KERNEL_AUTO) {
     if (!simt_ok) return fail(KAIRO_STATUS_NOT_SUPPORTED, kernel == KAIRO_KERNEL_AUTO ? why_tc + "; " + why_simt : why_simt);
@@ -123,6 +151,7 @@ kairo_status choose(const kairo_bsr* a, const void* b, int64_t ldb, int32_t layo
 // so memory that one call uses for other data is never another call's counter.
 size_t ws_bytes_for(const Choice& ch) {
   if (ch.path == Path::kTc) return ch.plan.workspace_bytes;
+  if (ch.path == Path::kBand) return ch.band.workspace_bytes;
   return kWorkspaceHeaderBytes + kCounterRegionBytes;
 }
 
@@ -162,9 +191,10 @@ const char* kairo_last_error_message(void) { return g_last_error.c_str(); }
 
 int32_t kairo_abi_version(void) { return KAIRO_ABI_VERSION; }
 
-kairo_status kairo_bsr_spmm_workspace_size(const kairo_bsr* a, int32_t layout, int64_t n,
-                                           const kairo_spmm_config* cfg, size_t* bytes) {
-  if (!bytes || !a) return fail(KAIRO_STATUS_INVALID_VALUE, "null argument");
+namespace {
+
+// The path kairo_bsr_spmm would take for `a`, with aligned dummy operands.
+kairo_status probe_choice(const kairo_bsr* a, int32_t layout, int64_t n, const kairo_spmm_config* cfg, Choice* ch) {
   // Pointer-alignment checks cannot be made without the operands; assume
   // aligned operands (the size only grows on the tcgen05 path).
   kairo_bsr probe = *a;
@@ -172,13 +202,65 @@ kairo_status kairo_bsr_spmm_workspace_size(const kairo_bsr* a, int32_t layout, i
   if (!probe.blocks) probe.blocks = dummy;
   if (!probe.row_ptr) probe.row_ptr = reinterpret_cast<const int32_t*>(dummy);
   if (!probe.col_idx) probe.col_idx = reinterpret_cast<const int32_t*>(dummy);
-  Choice ch;
   const int64_t ldb = layout == KAIRO_LAYOUT_STANDARD ? ((n + 7) / 8) * 8 : ((a->cols + 7) / 8) * 8;
   const int64_t ldc = layout == KAIRO_LAYOUT_STANDARD ? n : a->rows;
   const kairo_dtype c_dtype = KAIRO_DTYPE_F32;
-  kairo_status st = choose(&probe, dummy, ldb, layout, n, dummy, ldc, c_dtype, cfg, &ch);
+  return choose(&probe, dummy, ldb, layout, n, dummy, ldc, c_dtype, cfg, ch);
+}
+
+}  // namespace
+
+kairo_status kairo_bsr_spmm_workspace_size(const kairo_bsr* a, int32_t layout, int64_t n,
+                                           const kairo_spmm_config* cfg, size_t* bytes) {
+  if (!bytes || !a) return fail(KAIRO_STATUS_INVALID_VALUE, "null argument");
+  Choice ch;
+  kairo_status st = probe_choice(a, layout, n, cfg, &ch);
   if (st) return st;
   *bytes = ws_bytes_for(ch);
+  return KAIRO_STATUS_SUCCESS;
+}
+
+kairo_status kairo_bsr_spmm_describe(const kairo_bsr* a, int32_t layout, int64_t n, const kairo_spmm_config* cfg,
+                                     kairo_spmm_plan* out) {
+  if (!out || !a) return fail(KAIRO_STATUS_INVALID_VALUE, "null argument");
+  Choice ch;
+  kairo_status st = probe_choice(a, layout, n, cfg, &ch);
+  if (st) return st;
+  kairo_spmm_plan p{};
+  p.workspace_bytes = ws_bytes_for(ch);
+  switch (ch.path) {
+    case Path::kNone:
+      break;
+    case Path::kZero:
+      p.launches = 1;
+      break;
+    case Path::kSimt:
+      p.kernel = KAIRO_KERNEL_SIMT;
+      p.launches = 1;
+      p.n_tile = 128;
+      break;
+    case Path::kTc:
+      p.kernel = KAIRO_KERNEL_TCGEN05;
+      p.schedule = KAIRO_SCHEDULE_ROWS;
+      p.launches = 1;
+      p.grid = ch.plan.grid;
+      p.n_tile = 128 * ch.plan.nt;
+      p.stages = ch.plan.stages;
+      p.group_blocks = ch.plan.group;
+      p.rows = ch.plan.row_cost;
+      break;
+    case Path::kBand:
+      p.kernel = KAIRO_KERNEL_TCGEN05;
+      p.schedule = KAIRO_SCHEDULE_BANDS;
+      p.launches = 2;
+      p.grid = ch.band.grid;
+      p.n_tile = 128 * ch.band.nt;
+      p.stages = ch.band.stages;
+      p.group_blocks = ch.band.group;
+      p.rows = ch.band.rows;
+      break;
+  }
+  *out = p;
   return KAIRO_STATUS_SUCCESS;
 }
 
@@ -204,6 +286,7 @@ kairo_status kairo_bsr_spmm(const kairo_bsr* a, const void* b, int64_t ldb, int3
     return fail(KAIRO_STATUS_WORKSPACE_TOO_SMALL, os.str());
   }
   if (ch.path == Path::kTc) return tc_launch(a, b, ldb, layout, n, c, ldc, c_dtype, ch.plan, workspace, s);
+  if (ch.path == Path::kBand) return band_launch(a, b, ldb, layout, n, c, ldc, c_dtype, ch.band, workspace, s);
   return simt_launch(a, b, ldb, n, c, ldc, workspace, s);
 }
 
@@ -292,8 +375,10 @@ kairo_status kairo_acc_spmm_forward(const void* a_tiles, const int32_t* tile_row
   int32_t* col_idx = reinterpret_cast<int32_t*>(ws + L.col_idx_off);
   int32_t* perm = reinterpret_cast<int32_t*>(ws + L.perm_off);
   int32_t identity = 0;
+  // max_row_blocks stays 0 (row-split schedule): the workspace was sized before
+  // the build, without knowing the row lengths.
   st = kairo_bsr_build(tile_row_ids, tile_col_ids, num_tiles, L.nbr, L.nbc, row_ptr, col_idx, perm, &identity,
-                       ws + L.build_off, L.total - L.build_off, stream);
+                       nullptr, ws + L.build_off, L.total - L.build_off, stream);
   if (st) return st;
   kairo_bsr a{};
   a.rows = m;

@@ -46,16 +46,10 @@
 
 #include "internal.h"
 #include "ptx.cuh"
+#include "tc_common.cuh"
 
 namespace kairo {
 namespace {
-
-constexpr int kThreads = 192;
-constexpr long long kWaitCycles = 8000000000LL;  // per-wait bound in SM cycles (about 4 s at 2 GHz)
-constexpr int kMaxSmem = 227 * 1024;
-
-// Wait-site tags recorded with a timeout (bits 8..15 of the error word).
-enum : uint32_t { kTagEmpty = 1, kTagFull = 2, kTagTmemEmpty = 3, kTagTmemFull = 4, kTagDrain = 5 };
 
 enum RowKind : int { kSkip = 0, kZero = 1, kDirect = 2, kPartial = 3 };
 
@@ -67,6 +61,7 @@ struct TcArgs {
   int64_t ldc;
   int64_t w;               // path units per chunk
   int64_t nblocks_stored;
+  int64_t nnzb;
   unsigned* err;
   unsigned* counters;      // this launch's bank: [ngroups][grid]
   unsigned* counters_other;  // the other bank, zeroed by this launch
@@ -193,81 +188,6 @@ __device__ __forceinline__ bool walk_items(const TcArgs& a, int64_t s, int64_t e
   return true;
 }
 
-template <typename TOut>
-__device__ __forceinline__ void store_scalar(TOut* p, float v);
-template <>
-__device__ __forceinline__ void store_scalar<float>(float* p, float v) { __stcs(p, v); }
-template <>
-__device__ __forceinline__ void store_scalar<__nv_bfloat16>(__nv_bfloat16* p, float v) {
-  *p = __float2bfloat16_rn(v);
-}
-template <>
-__device__ __forceinline__ void store_scalar<__half>(__half* p, float v) { *p = __float2half_rn(v); }
-
-// Writes 16 accumulator values of one thread: rows/cols as described in the
-// file header.  `col` is this thread's column of C (STANDARD) or row of Y
-// (LINEAR); rows j0..j0+15 of block-row i.
-template <bool LINEAR, typename TOut>
-__device__ __forceinline__ void store16(const TcArgs& a, int i, int bm, int j0, int col,
-                                        const float* v) {
-  if (col >= a.n) return;
-  const int row0 = i * bm + j0;
-  if (!LINEAR) {
-    float* c = static_cast<float*>(a.c);
-#pragma unroll
-    for (int jj = 0; jj < 16; ++jj) {
-      const int r = row0 + jj;
-      if (r < a.m) __stcs(c + static_cast<int64_t>(r) * a.ldc + col, v[jj]);
-    }
-  } else {
-    TOut* y = static_cast<TOut*>(a.c) + static_cast<int64_t>(col) * a.ldc + row0;
-    if (a.vec_store && row0 + 16 <= a.m) {
-      if constexpr (sizeof(TOut) == 4) {
-        float4* y4 = reinterpret_cast<float4*>(y);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) y4[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-      } else {
-        uint32_t w[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          TOut lo, hi;
-          store_scalar<TOut>(&lo, v[2 * q]);
-          store_scalar<TOut>(&hi, v[2 * q + 1]);
-          w[q] = static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&lo)) |
-                 (static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&hi)) << 16);
-        }
-        uint4* y4 = reinterpret_cast<uint4*>(y);
-        y4[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        y4[1] = make_uint4(w[4], w[5], w[6], w[7]);
-      }
-    } else {
-#pragma unroll
-      for (int jj = 0; jj < 16; ++jj)
-        if (row0 + jj < a.m) store_scalar<TOut>(y + jj, v[jj]);
-    }
-  }
-}
-
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
-// OR of `pred` over the 128 epilogue threads (named barrier 1).  Used so that
-// the four epilogue warps always leave the work loop at the same item; a warp
-// that left alone would strand the others at the next named barrier.
-__device__ __forceinline__ bool epi_any(bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t"
-      ".reg .pred p, q;\n\t"
-      "setp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.or.pred q, 1, 128, p;\n\t"
-      "selp.u32 %0, 1, 0, q;\n\t"
-      "}"
-      : "=r"(r)
-      : "r"(static_cast<uint32_t>(pred))
-      : "memory");
-  return r != 0;
-}
-
 template <int BM, int BK, int NT, bool LINEAR, int IN_FMT, typename TOut>
 __global__ void __launch_bounds__(kThreads, 1)
     bsr_spmm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
@@ -356,21 +276,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     int gpos = 0;      // next slot in the current group
     int gidx = 0;      // stage of the current group
     uint32_t gph = 0;  // phase of that stage
+    IndexWindow win;
     walk_items(args, s_range, e_range, i_start, lane, [&](const RowItem& it) -> bool {
       if (it.kind != kDirect && it.kind != kPartial) return true;
       const int n0 = it.chunk * NT * 128;
       for (int pb = it.p0; pb < it.p1; pb += 32) {
         const int cnt = min(32, it.p1 - pb);
         int mc = 0, mb = 0;
+        win.ensure(args.col_idx, args.blk_idx, args.nnzb, pb, lane);
+        win.get(pb + lane, mc, mb);
         if (lane < cnt) {
-          mc = __ldg(args.col_idx + pb + lane);
-          mb = args.blk_idx ? __ldg(args.blk_idx + pb + lane) : pb + lane;
           if (static_cast<unsigned>(mc) >= static_cast<unsigned>(args.nbc) ||
               mb < 0 || static_cast<int64_t>(mb) >= args.nblocks_stored) {
             atomicCAS(args.err, 0u, KAIRO_DEVERR_BAD_INDEX);
             mc = 0;
             mb = 0;
           }
+        } else {
+          mc = 0;
+          mb = 0;
         }
         int j0 = 0;
         while (j0 < cnt) {
@@ -587,73 +511,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------- host side
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
-CUtensorMapSwizzle swizzle_for_bytes(int inner_bytes) {
-  return inner_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
-         : inner_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
-                             : CU_TENSOR_MAP_SWIZZLE_32B;
-}
-
-kairo_status make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes,
-                         uint64_t inner, uint64_t outer, uint64_t row_stride_elems, uint32_t box_inner,
-                         uint32_t box_outer, const char* what) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return fail(KAIRO_STATUS_CUDA_ERROR, "cuTensorMapEncodeTiled is not available from the driver");
-  const cuuint64_t dims[2] = {inner, outer};
-  const cuuint64_t strides[1] = {row_stride_elems * static_cast<uint64_t>(elem_bytes)};
-  const cuuint32_t box[2] = {box_inner, box_outer};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  swizzle_for_bytes(static_cast<int>(box_inner) * elem_bytes), CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    std::ostringstream os;
-    os << "cuTensorMapEncodeTiled failed for " << what << " (CUresult " << static_cast<int>(r) << ")";
-    return fail(KAIRO_STATUS_INVALID_VALUE, os.str());
-  }
-  return KAIRO_STATUS_SUCCESS;
-}
-
-// B (K x N, row stride ldb) viewed as [N/64][K][64] so that one box of
-// (64, bk, atoms) brings a whole panel in the MN-major 128B-swizzled layout.
-kairo_status make_map_b3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t n, uint64_t k,
-                          uint64_t ldb, uint32_t bk, uint32_t atoms) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return fail(KAIRO_STATUS_CUDA_ERROR, "cuTensorMapEncodeTiled is not available from the driver");
-  const cuuint64_t dims[3] = {64, k, n / 64};
-  const cuuint64_t strides[2] = {ldb * 2, 128};
-  const cuuint32_t box[3] = {64, bk, atoms};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    std::ostringstream os;
-    os << "cuTensorMapEncodeTiled failed for the 3D view of B (CUresult " << static_cast<int>(r) << ")";
-    return fail(KAIRO_STATUS_INVALID_VALUE, os.str());
-  }
-  return KAIRO_STATUS_SUCCESS;
-}
-
-constexpr int stage_bytes(int bm, int bk, int nt) {
-  return nt * 128 * bk * 2 + (bm * bk * 2 + 1023) / 1024 * 1024;
-}
-
 using KernelFn = void (*)(CUtensorMap, CUtensorMap, TcArgs);
 
 template <int BM, int NT, bool LINEAR, int IN_FMT, typename TOut>
@@ -777,15 +634,7 @@ kairo_status tc_plan(const kairo_bsr* a, int32_t layout, int64_t n, const kairo_
   const int budget = kMaxSmem - reserve;
   int group = (cfg && cfg->group_blocks > 0) ? cfg->group_blocks : 0;
   if (group > 32) return fail(KAIRO_STATUS_INVALID_VALUE, "group_blocks must be at most 32");
-  if (group == 0) {
-    const int cand[] = {8, 6, 4, 3, 2, 1};
-    group = 1;
-    for (int g : cand)
-      if (budget / (g * sb) >= 4) {
-        group = g;
-        break;
-      }
-  }
+  if (group == 0) group = default_group_blocks(budget / sb, b_slice_bytes(a, nt) > 0.5 * device_l2_bytes(device));
   int max_stages = budget / (group * sb);
   if (max_stages > 32) max_stages = 32;
   int stages = (cfg && cfg->stages > 0) ? std::min(cfg->stages, max_stages) : max_stages;
@@ -811,28 +660,9 @@ kairo_status tc_launch(const kairo_bsr* a, const void* b, int64_t ldb, int32_t l
   const bool linear = layout == KAIRO_LAYOUT_LINEAR;
   KernelFn fn = pick_kernel(plan.bm, plan.nt, linear, a->dtype, c_dtype);
   if (!fn) return fail(KAIRO_STATUS_NOT_SUPPORTED, "no tcgen05 kernel for this block size / dtype combination");
-  const CUtensorMapDataType dt =
-      a->dtype == KAIRO_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap map_a, map_b;
-  kairo_status st = make_map_2d(&map_a, a->blocks, dt, 2, static_cast<uint64_t>(a->bk),
-                                static_cast<uint64_t>(a->nblocks_stored) * a->bm, static_cast<uint64_t>(a->bk),
-                                static_cast<uint32_t>(a->bk), static_cast<uint32_t>(a->bm), "block storage");
-  if (st) return st;
   int b_box3d = 0;
-  if (!linear) {
-    if (n % 64 == 0) {
-      st = make_map_b3d(&map_b, b, dt, static_cast<uint64_t>(n), static_cast<uint64_t>(a->cols),
-                        static_cast<uint64_t>(ldb), static_cast<uint32_t>(a->bk), static_cast<uint32_t>(2 * plan.nt));
-      b_box3d = (st == KAIRO_STATUS_SUCCESS);
-    }
-    if (!b_box3d)
-      st = make_map_2d(&map_b, b, dt, 2, static_cast<uint64_t>(n), static_cast<uint64_t>(a->cols),
-                       static_cast<uint64_t>(ldb), 64, static_cast<uint32_t>(a->bk), "B");
-  } else {
-    st = make_map_2d(&map_b, b, dt, 2, static_cast<uint64_t>(a->cols), static_cast<uint64_t>(n),
-                     static_cast<uint64_t>(ldb), static_cast<uint32_t>(a->bk), static_cast<uint32_t>(128 * plan.nt),
-                     "X");
-  }
+  kairo_status st = make_operand_maps(a, b, ldb, linear, n, plan.nt, &map_a, &map_b, &b_box3d);
   if (st) return st;
 
   TcArgs args{};
@@ -843,6 +673,7 @@ kairo_status tc_launch(const kairo_bsr* a, const void* b, int64_t ldb, int32_t l
   args.ldc = ldc;
   args.w = plan.w;
   args.nblocks_stored = a->nblocks_stored;
+  args.nnzb = a->nnzb;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   args.err = reinterpret_cast<unsigned*>(ws);
   const int bank = next_counter_bank(workspace);

@@ -14,6 +14,7 @@ from kairo_b200.ops.spmm import (
     block_sparse_mm_bsr,
     bsr_from_mask,
     bsr_from_tiles,
+    describe,
     sparse_linear,
 )
 
@@ -34,6 +35,7 @@ __all__ = [
     "block_sparse_mm_bsr",
     "bsr_from_mask",
     "bsr_from_tiles",
+    "describe",
     "sparse_linear",
     "KernelConfig",
     "TileAutotuner",

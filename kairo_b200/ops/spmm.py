@@ -29,9 +29,12 @@ class KernelConfig:
 
     kernel: "auto", "simt" or "tcgen05"; n_tile: C columns per work item on
     the tcgen05 kernel (128 or 256); stages: pipeline stages in shared
-    memory; row_cost: scheduler weight of a block-row in units of one block;
-    num_ctas: persistent grid size; group_blocks: nonzero blocks loaded per
-    pipeline stage (1..32).
+    memory; row_cost: scheduler weight of a block-row in units of one block
+    (row-split schedule); num_ctas: persistent grid size; group_blocks:
+    nonzero blocks loaded per pipeline stage (1..32); schedule: "auto",
+    "rows" (block-rows split over CTAs, robust to skew) or "bands" (CTAs
+    sweep B panels together, for a B slice larger than L2); band_rows:
+    block-rows per band item.
     """
 
     kernel: str = "auto"
@@ -40,13 +43,17 @@ class KernelConfig:
     row_cost: int = 0
     num_ctas: int = 0
     group_blocks: int = 0
+    schedule: str = "auto"
+    band_rows: int = 0
 
     def __post_init__(self) -> None:
         if self.kernel not in ("auto", "simt", "tcgen05"):
             raise ValueError(f"kernel must be 'auto', 'simt' or 'tcgen05', got {self.kernel!r}")
         if self.n_tile not in (0, 128, 256):
             raise ValueError(f"n_tile must be 0, 128 or 256, got {self.n_tile}")
-        for name in ("stages", "row_cost", "num_ctas", "group_blocks"):
+        if self.schedule not in ("auto", "rows", "bands"):
+            raise ValueError(f"schedule must be 'auto', 'rows' or 'bands', got {self.schedule!r}")
+        for name in ("stages", "row_cost", "num_ctas", "group_blocks", "band_rows"):
             if getattr(self, name) < 0:
                 raise ValueError(f"{name} must be non-negative")
         if self.group_blocks > 32:
@@ -60,6 +67,8 @@ class KernelConfig:
         c.row_cost = self.row_cost
         c.num_ctas = self.num_ctas
         c.group_blocks = self.group_blocks
+        c.schedule = {"auto": _lib.SCHEDULE_AUTO, "rows": _lib.SCHEDULE_ROWS, "bands": _lib.SCHEDULE_BANDS}[self.schedule]
+        c.band_rows = self.band_rows
         return c
 
 
@@ -169,12 +178,14 @@ def bsr_from_tiles(
         _lib.check(lib.kairo_bsr_build_workspace_size(nt, nbr, ctypes.byref(nbytes)), "bsr_from_tiles")
         ws = torch.empty(max(nbytes.value, 256), dtype=torch.uint8, device=dev)
         ident = ctypes.c_int32(0)
+        longest = ctypes.c_int32(0)
         _lib.check(lib.kairo_bsr_build(rows.data_ptr() if nt else None, cols.data_ptr() if nt else None, nt, nbr,
                                        nbc, row_ptr.data_ptr(), col_idx.data_ptr() if nt else None,
-                                       perm.data_ptr() if nt else None, ctypes.byref(ident), ws.data_ptr(),
-                                       ws.numel(), _lib.stream_handle(dev)), "bsr_from_tiles")
+                                       perm.data_ptr() if nt else None, ctypes.byref(ident), ctypes.byref(longest),
+                                       ws.data_ptr(), ws.numel(), _lib.stream_handle(dev)), "bsr_from_tiles")
     return BlockSparseMatrix(row_ptr=row_ptr, col_idx=col_idx, blocks=tiles.contiguous(), shape=(m, k),
-                             block_size=(bm, bk), blk_idx=None if ident.value else perm)
+                             block_size=(bm, bk), blk_idx=None if ident.value else perm,
+                             max_row_blocks=int(longest.value))
 
 
 def bsr_from_mask(A: Tensor, block_mask: SparseMask, tile_size: int) -> BlockSparseMatrix:
@@ -195,7 +206,27 @@ def _bsr_desc(a: BlockSparseMatrix) -> _lib.KairoBsr:
     d.blk_idx = a.blk_idx.data_ptr() if a.blk_idx is not None and a.nnzb else None
     d.blocks = a.blocks.data_ptr() if a.blocks.numel() else None
     d.dtype = _lib.kairo_dtype(a.dtype)
+    d.max_row_blocks = a.max_row_blocks
     return d
+
+
+def describe(a: BlockSparseMatrix, n: int, *, linear: bool = False, config: KernelConfig | None = None) -> dict:
+    """What ``block_sparse_mm_bsr`` (``linear=False``) or ``sparse_linear``
+    (``linear=True``, N = rows of X) would run for ``a``: kernel, schedule,
+    kernel launches per call, grid and pipeline shape, workspace bytes."""
+    lib = _lib.lib()
+    plan = _lib.KairoSpmmPlan()
+    desc = _bsr_desc(a)
+    cfg = (config or KernelConfig()).to_c()
+    layout = _lib.LAYOUT_LINEAR if linear else _lib.LAYOUT_STANDARD
+    with torch.cuda.device(a.device):
+        _lib.check(lib.kairo_bsr_spmm_describe(ctypes.byref(desc), layout, int(n), ctypes.byref(cfg),
+                                               ctypes.byref(plan)), "describe")
+    kernel = {0: "none", _lib.KERNEL_SIMT: "simt", _lib.KERNEL_TCGEN05: "tcgen05"}[plan.kernel]
+    schedule = {0: "none", _lib.SCHEDULE_ROWS: "rows", _lib.SCHEDULE_BANDS: "bands"}[plan.schedule]
+    return {"kernel": kernel, "schedule": schedule, "launches": plan.launches, "grid": plan.grid,
+            "n_tile": plan.n_tile, "stages": plan.stages, "group_blocks": plan.group_blocks, "rows": plan.rows,
+            "workspace_bytes": int(plan.workspace_bytes)}
 
 
 def _launch(a: BlockSparseMatrix, b: Tensor, ldb: int, layout: int, n: int, out: Tensor, ldc: int,

@@ -79,7 +79,7 @@ def shard_bsr(a: BlockSparseMatrix, rank: int, world_size: int,
         blocks = a.blocks
         blk = a.blk_idx[n0:n1]
     shard = BlockSparseMatrix(row_ptr=sub_rp, col_idx=col, blocks=blocks, shape=(rows, k), block_size=(bm, bk),
-                              blk_idx=blk)
+                              blk_idx=blk, max_row_blocks=a.max_row_blocks)
     return shard, RowShard(rank, world_size, r0, r1, n0, n1, bm)
 
 

@@ -63,6 +63,9 @@ class BlockSparseMatrix:
         block_size: (bm, bk).
         blk_idx: optional (nnzb,) int32; block p is ``blocks[blk_idx[p]]``.
             ``None`` means block p is ``blocks[p]``.
+        max_row_blocks: length of the longest block-row, when known (0 =
+            unknown).  Informational (passed to the C ABI with the matrix);
+            ``bsr_from_tiles`` fills it in; ``shard_bsr`` carries it over.
     """
 
     row_ptr: torch.Tensor
@@ -71,6 +74,7 @@ class BlockSparseMatrix:
     shape: tuple[int, int]
     block_size: tuple[int, int]
     blk_idx: torch.Tensor | None = None
+    max_row_blocks: int = 0
 
     def __post_init__(self) -> None:
         m, k = self.shape
@@ -90,6 +94,8 @@ class BlockSparseMatrix:
             raise ValueError(f"blocks must be (n, {bm}, {bk}), got {tuple(self.blocks.shape)}")
         if self.blk_idx is None and self.blocks.shape[0] < self.col_idx.numel():
             raise ValueError("fewer stored blocks than nonzero blocks")
+        if self.max_row_blocks < 0:
+            raise ValueError("max_row_blocks must be non-negative")
 
     @property
     def nbr(self) -> int:

@@ -24,7 +24,7 @@ def declared_symbols() -> list[str]:
 def test_library_builds_for_sm100a_and_loads():
     assert "arch=compute_100a,code=sm_100a" in " ".join(_build.ARCH_FLAGS)
     lib = _lib.lib()
-    assert lib.kairo_abi_version() == 1
+    assert lib.kairo_abi_version() == _lib.ABI_VERSION == 2
 
 
 def test_every_declared_symbol_is_exported():
