@@ -432,7 +432,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             alive = false;
             break;
           }
-          ptx::tc_fence_after();
           slot16 = static_cast<uint32_t>(midx * GB) * SLOT16;
         }
         const int seg = min(total - i, GB - mpos);

@@ -369,10 +369,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int p = it.p0;
       while (p < it.p1) {
         if (mpos == 0) {
+          // No tcgen05 fence here: the MMAs read shared memory the TMA wrote,
+          // and the mbarrier wait itself orders them after those writes.
           ok = ptx::wait_parity(&full[midx], mph, abort_flag, args.err, kTagFull, kWaitCycles);
           ok = __shfl_sync(0xffffffffu, ok, 0);
           if (!ok) return false;
-          ptx::tc_fence_after();
           slot16 = static_cast<uint32_t>(midx * GB) * SLOT16;
         }
         // Blocks [p, p + seg) all live in the current stage group.
