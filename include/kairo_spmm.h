@@ -91,7 +91,7 @@ typedef struct kairo_bsr {
   const int32_t* blk_idx;    /* nnzb, or NULL for identity */
   const void* blocks;        /* (nblocks_stored, bm, bk) row-major, dtype below */
   kairo_dtype dtype;
-  int32_t max_row_blocks;    /* longest block-row in blocks, if known (0 = unknown); informational */
+  int32_t max_row_blocks;    /* longest block-row in blocks, if known (0 = unknown); a scheduling hint */
 } kairo_bsr;
 
 /* Tuning knobs of one launch; zero-initialised means "library default". */
@@ -114,7 +114,10 @@ typedef struct kairo_spmm_config {
  * BANDS: each CTA holds `band_rows` block-rows in TMEM and visits their
  *        blocks in column order, all CTAs sweeping B together so gathered B
  *        panels are shared through L2.  Rows are never cut.
- * AUTO picks ROWS. */
+ * AUTO picks BANDS when a chunk has fewer block-rows than twice the SM
+ * count (the row-split schedule would cut most rows), there are at least
+ * four band items per SM, and kairo_bsr.max_row_blocks shows rows of
+ * similar length; otherwise ROWS. */
 typedef enum kairo_schedule {
   KAIRO_SCHEDULE_AUTO = 0,
   KAIRO_SCHEDULE_ROWS = 1,

@@ -107,6 +107,7 @@ struct BandPlan {
 
 // Band schedule (spmm_band.cu)
 bool band_supported(const kairo_bsr* a, std::string* why);
+bool band_preferred(const kairo_bsr* a, int64_t n, int device);
 kairo_status band_plan(const kairo_bsr* a, int32_t layout, int64_t n, const kairo_spmm_config* cfg,
                        int device, BandPlan* plan);
 kairo_status band_launch(const kairo_bsr* a, const void* b, int64_t ldb, int32_t layout, int64_t n,

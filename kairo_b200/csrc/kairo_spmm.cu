@@ -127,9 +127,9 @@ kairo_status choose(const kairo_bsr* a, const void* b, int64_t ldb, int32_t layo
     if (!tc_ok) return fail(KAIRO_STATUS_NOT_SUPPORTED, why_tc);
     const int dev = current_device();
     std::string why_band;
-    if (schedule == KAIRO_SCHEDULE_BANDS && !band_supported(a, &why_band))
-      return fail(KAIRO_STATUS_NOT_SUPPORTED, why_band);
-    if (schedule == KAIRO_SCHEDULE_BANDS) {
+    const bool band_ok = band_supported(a, &why_band);
+    if (schedule == KAIRO_SCHEDULE_BANDS && !band_ok) return fail(KAIRO_STATUS_NOT_SUPPORTED, why_band);
+    if (schedule == KAIRO_SCHEDULE_BANDS || (schedule == KAIRO_SCHEDULE_AUTO && band_ok && band_preferred(a, n, dev))) {
       ch.path = Path::kBand;
       st = band_plan(a, layout, n, cfg, dev, &ch.band);
     } else {

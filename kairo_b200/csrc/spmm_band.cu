@@ -597,6 +597,25 @@ bool band_supported(const kairo_bsr* a, std::string* why) {
   return true;
 }
 
+bool band_preferred(const kairo_bsr* a, int64_t n, int device) {
+  // The row-split schedule cuts a block-row wherever a CTA's share of the
+  // merge path ends and sums the pieces through partial tiles.  When a chunk
+  // has fewer block-rows than twice the CTAs, most rows are cut (the linear
+  // layer: 128 rows, 148 CTAs, 1.54 ms) and the band schedule, which keeps
+  // rows whole, is faster (1.40 ms).  It needs enough items to balance the
+  // CTAs and rows of similar length, which only the caller's max_row_blocks
+  // can vouch for.
+  if (a->max_row_blocks <= 0 || a->nbr <= 0 || a->nnzb <= 0) return false;
+  const int sms = device_sm_count(device);
+  if (a->nbr >= 2 * sms) return false;
+  const double mean = static_cast<double>(a->nnzb) / a->nbr;
+  if (a->max_row_blocks > 2.0 * mean + 8.0) return false;
+  const int nt = n > 128 ? 2 : 1;
+  const int R = std::max(1, std::min(kMaxBandRows, 256 / (nt * a->bm)));
+  const int64_t nitems = ceil_div64(n, 128 * nt) * ceil_div64(a->nbr, R);
+  return nitems >= 4 * static_cast<int64_t>(sms);
+}
+
 kairo_status band_plan(const kairo_bsr* a, int32_t layout, int64_t n, const kairo_spmm_config* cfg, int device,
                        BandPlan* plan) {
   (void)layout;
@@ -611,7 +630,9 @@ kairo_status band_plan(const kairo_bsr* a, int32_t layout, int64_t n, const kair
   p.nt = nt;
   p.nchunks = static_cast<int>(ceil_div64(n, 128 * nt));
   const int row_cols = nt * p.bm;
-  int R = (cfg && cfg->band_rows > 0) ? cfg->band_rows : 512 / row_cols;
+  // Default: the most rows that still leave room for two accumulator sets,
+  // so the epilogue of one item overlaps the MMAs of the next.
+  int R = (cfg && cfg->band_rows > 0) ? cfg->band_rows : std::max(1, 256 / row_cols);
   if (R > kMaxBandRows) R = kMaxBandRows;
   if (R * row_cols > 512) return fail(KAIRO_STATUS_INVALID_VALUE, "band_rows * n_tile/128 * block size exceeds TMEM");
   if (R > a->nbr && a->nbr > 0) R = a->nbr;

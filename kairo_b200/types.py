@@ -64,7 +64,8 @@ class BlockSparseMatrix:
         blk_idx: optional (nnzb,) int32; block p is ``blocks[blk_idx[p]]``.
             ``None`` means block p is ``blocks[p]``.
         max_row_blocks: length of the longest block-row, when known (0 =
-            unknown).  Informational (passed to the C ABI with the matrix);
+            unknown).  A scheduling hint: the band schedule is chosen
+            automatically only when it shows rows of similar length.
             ``bsr_from_tiles`` fills it in; ``shard_bsr`` carries it over.
     """
 

@@ -143,15 +143,24 @@ def _uniform_rows_matrix(nbr, nbc, per_row, bs, max_row_blocks):
 
 
 def test_schedule_choice():
-    """AUTO runs the row-split schedule, also for a B slice larger than L2
-    (the band schedule is slower there on B200); "bands" is taken when asked."""
-    # B slice of a 256-column chunk: 262144 x 256 x 2 B = 134 MB > L2
+    """AUTO picks the band schedule only when a chunk has fewer block-rows than
+    twice the SMs (the row-split schedule would cut most rows), with enough
+    items and a row-length hint showing similar rows; otherwise rows."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    # many short rows (the 262144^2 case): rows
     a = _uniform_rows_matrix(1024, 8192, 41, 32, max_row_blocks=41)
     assert describe(a, 1024)["schedule"] == "rows"
     assert describe(a, 1024, config=KernelConfig(schedule="bands"))["schedule"] == "bands"
     plan = describe(a, 1024)
     # B slice above half of L2: four pipeline stages of three 18 KB slots
     assert (plan["stages"], plan["group_blocks"]) == (4, 3)
+    # few long rows, many chunks (the linear layer): bands
+    few = max(1, sms // 2)
+    b = _uniform_rows_matrix(few, 512, 100, 64, max_row_blocks=100)
+    assert describe(b, 8192)["schedule"] == "bands"
+    # ... but not without the row-length hint, nor with a very long row
+    assert describe(_uniform_rows_matrix(few, 512, 100, 64, max_row_blocks=0), 8192)["schedule"] == "rows"
+    assert describe(_uniform_rows_matrix(few, 512, 100, 64, max_row_blocks=400), 8192)["schedule"] == "rows"
     a2 = _uniform_rows_matrix(1024, 512, 41, 32, max_row_blocks=41)
     plan2 = describe(a2, 1024)
     assert plan2["schedule"] == "rows" and (plan2["stages"], plan2["group_blocks"]) == (3, 4)
