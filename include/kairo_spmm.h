@@ -202,6 +202,52 @@ KAIRO_API kairo_status kairo_bsr_build(const int32_t* tile_row_ids, const int32_
 KAIRO_API kairo_status kairo_bsr_build_workspace_size(int64_t num_tiles, int32_t nbr, size_t* bytes);
 
 /* ------------------------------------------------------------------------
+ * BSR transpose on the device, for the backward pass of the linear layer
+ * (dX = dY * W is the LINEAR-layout product with W^T).  No counterpart in
+ * the reference, which has no SpMM backward.
+ *
+ * W^T has cols/bk block-rows and the same blocks, each transposed (bk x bm).
+ * Its order is the stable sort of W's positions by block-column, i.e.
+ * (column, row) order, the BSR convention applied to W^T's COO list.
+ *   row_ptr_t  (cols/bk + 1)   block-row offsets of W^T;
+ *   col_idx_t  (nnzb)          block-columns of W^T (block-rows of W);
+ *   perm_t     (nnzb)          W's BSR position of every W^T position;
+ *   blocks_t   (nnzb, bk, bm)  transposed blocks in W^T order, W's dtype
+ *                              (NULL: structure only).
+ * Asynchronous on `stream` (no host synchronisation).  Invalid ids, or a
+ * block-column of more than 16384 blocks, are reported in the workspace
+ * error word (kairo_workspace_error), not by the return value.
+ * kairo_bsr_transpose_values refreshes blocks_t alone from a cached perm_t
+ * when only the values of W changed (a workspace of >= 256 bytes holds the
+ * error word).
+ * ---------------------------------------------------------------------- */
+KAIRO_API kairo_status kairo_bsr_transpose(const kairo_bsr* a, int32_t* row_ptr_t, int32_t* col_idx_t,
+                                           int32_t* perm_t, void* blocks_t, void* workspace,
+                                           size_t workspace_bytes, void* stream);
+KAIRO_API kairo_status kairo_bsr_transpose_workspace_size(const kairo_bsr* a, size_t* bytes);
+KAIRO_API kairo_status kairo_bsr_transpose_values(const kairo_bsr* a, const int32_t* perm_t, void* blocks_t,
+                                                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Weight gradient of the linear layer Y = X * W^T restricted to W's nonzero
+ * blocks (block-sampled dense x dense product).  No counterpart in the
+ * reference.  For every BSR position p = (block-row i, block-column j):
+ *   dblocks[p] = dY[:, i*bm : (i+1)*bm]^T * X[:, j*bk : (j+1)*bk]   (bm x bk)
+ * summed over the n batch rows; dY is (n x rows), X is (n x cols), both
+ * row-major with leading dimensions lddy / ldx, W's dtype.  `a` is W (its
+ * col_idx is read; values are not); row_ptr_t / col_idx_t / perm_t are W's
+ * transposed structure from kairo_bsr_transpose.  dblocks is (nnzb, bm, bk)
+ * in W's BSR order, fp32 or W's dtype.  64 x 64 f16/bf16 blocks run on the
+ * tensor cores, other shapes and fp32 on CUDA cores.  Asynchronous; device
+ * errors go to the workspace error word.
+ * ---------------------------------------------------------------------- */
+KAIRO_API kairo_status kairo_bsr_sddmm(const kairo_bsr* a, const int32_t* row_ptr_t, const int32_t* col_idx_t,
+                                       const int32_t* perm_t, const void* dy, int64_t lddy, const void* x,
+                                       int64_t ldx, int64_t n, void* dblocks, kairo_dtype out_dtype,
+                                       void* workspace, size_t workspace_bytes, void* stream);
+KAIRO_API kairo_status kairo_bsr_sddmm_workspace_size(const kairo_bsr* a, size_t* bytes);
+
+/* ------------------------------------------------------------------------
  * Dense A (M x K, leading dimension lda) -> tiles (num_tiles, tile, tile) in
  * COO order, zero-padding tiles that cross the right/bottom edge.  Replaces
  * the per-tile host loop of _dense_to_block_sparse (kairo/ops/spmm.py:16-55).

@@ -143,6 +143,13 @@ _SIGNATURES = {
     "kairo_bsr_build": (c_int32, [c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p, c_void_p, c_void_p,
                                   POINTER(c_int32), POINTER(c_int32), c_void_p, c_size_t, c_void_p]),
     "kairo_bsr_build_workspace_size": (c_int32, [c_int64, c_int32, POINTER(c_size_t)]),
+    "kairo_bsr_transpose": (c_int32, [POINTER(KairoBsr), c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+                                      c_void_p]),
+    "kairo_bsr_transpose_workspace_size": (c_int32, [POINTER(KairoBsr), POINTER(c_size_t)]),
+    "kairo_bsr_transpose_values": (c_int32, [POINTER(KairoBsr), c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "kairo_bsr_sddmm": (c_int32, [POINTER(KairoBsr), c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
+                                  c_int64, c_int64, c_void_p, c_int32, c_void_p, c_size_t, c_void_p]),
+    "kairo_bsr_sddmm_workspace_size": (c_int32, [POINTER(KairoBsr), POINTER(c_size_t)]),
     "kairo_dense_to_tiles": (c_int32, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int32,
                                        c_int32, c_void_p, c_void_p]),
     "kairo_acc_spmm_forward": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,

@@ -163,10 +163,52 @@ __global__ void __launch_bounds__(1024) k_segsort(const int32_t* __restrict__ co
   }
 }
 
-__global__ void k_fill_zero(int* p, int64_t n) {
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-    p[i] = 0;
+// Block-row of every BSR position (out[p] = i for row_ptr[i] <= p < row_ptr[i+1]).
+// One warp per block-row; positions outside [0, nnzb) are skipped.
+__global__ void k_expand_rows(const int32_t* __restrict__ row_ptr, int32_t nbr, int64_t nnzb,
+                              int32_t* __restrict__ out) {
+  const int warps = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = blockIdx.x * static_cast<int64_t>(warps) + (threadIdx.x >> 5); r < nbr;
+       r += static_cast<int64_t>(gridDim.x) * warps) {
+    const int64_t p0 = max(static_cast<int64_t>(0), static_cast<int64_t>(row_ptr[r]));
+    const int64_t p1 = min(nnzb, static_cast<int64_t>(row_ptr[r + 1]));
+    for (int64_t p = p0 + lane; p < p1; p += 32) out[p] = static_cast<int32_t>(r);
+  }
+}
+
+// blocks_t[q] = transpose(blocks[stored(perm_t[q])]) for q < nnzb, through a
+// shared-memory tile so that both the read and the write are coalesced.
+// One CTA per output block (grid-stride); bm, bk <= 64.
+template <typename T>
+__global__ void __launch_bounds__(256) k_transpose_blocks(const T* __restrict__ blocks, const int32_t* __restrict__ blk_idx,
+                                                          const int32_t* __restrict__ perm_t, int64_t nnzb,
+                                                          int64_t nstored, int32_t bm, int32_t bk,
+                                                          T* __restrict__ out, unsigned* err) {
+  __shared__ T tile[64][65];
+  for (int64_t q = blockIdx.x; q < nnzb; q += gridDim.x) {
+    const int64_t p = perm_t[q];
+    int64_t s = (p >= 0 && p < nnzb) ? (blk_idx ? static_cast<int64_t>(blk_idx[p]) : p) : -1;
+    const bool ok = s >= 0 && s < nstored;
+    if (!ok && threadIdx.x == 0) atomicCAS(err, 0u, KAIRO_DEVERR_BAD_INDEX);
+    const T* src = blocks + (ok ? s : 0) * bm * bk;
+    for (int e = threadIdx.x; e < bm * bk; e += blockDim.x) {
+      const int r = e / bk, c = e - r * bk;
+      T v;
+      if (ok)
+        v = src[e];
+      else
+        memset(&v, 0, sizeof(T));
+      tile[r][c] = v;
+    }
+    __syncthreads();
+    T* dst = out + q * bm * bk;  // (bk x bm) row-major
+    for (int e = threadIdx.x; e < bm * bk; e += blockDim.x) {
+      const int c = e / bm, r = e - c * bm;
+      dst[e] = tile[r][c];
+    }
+    __syncthreads();
+  }
 }
 
 // Dense (M x K) -> tiles (num_tiles, tile, tile), zero-padded at the edges.
@@ -304,4 +346,143 @@ extern "C" kairo_status kairo_dense_to_tiles(const void* a, int64_t m, int64_t k
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch of the dense-to-tiles kernel");
   return KAIRO_STATUS_SUCCESS;
+}
+
+// ------------------------------------------------------------ transpose
+
+namespace kairo {
+namespace {
+
+// Transpose workspace: header (error word, flags), per-column counts and
+// fill counters, then the block-row of every BSR position.
+struct TransposeWs {
+  unsigned* err;
+  int* flags;
+  int* counts;
+  int* fill;
+  int32_t* rows_of_pos;
+};
+
+size_t transpose_ws_bytes(int64_t nnzb, int32_t nbc) {
+  const size_t col = align_up(static_cast<size_t>(nbc), 64) * sizeof(int);
+  return kWorkspaceHeaderBytes + 2 * col + align_up(static_cast<size_t>(nnzb), 64) * sizeof(int32_t);
+}
+
+TransposeWs carve_transpose(void* ws, int32_t nbc) {
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  TransposeWs w;
+  w.err = reinterpret_cast<unsigned*>(p);
+  w.flags = reinterpret_cast<int*>(p + 64);
+  const size_t col = align_up(static_cast<size_t>(nbc), 64);
+  w.counts = reinterpret_cast<int*>(p + kWorkspaceHeaderBytes);
+  w.fill = w.counts + col;
+  w.rows_of_pos = w.fill + col;
+  return w;
+}
+
+kairo_status transpose_values(const kairo_bsr* a, const int32_t* perm_t, void* blocks_t, unsigned* err,
+                              cudaStream_t s) {
+  if (a->nnzb == 0) return KAIRO_STATUS_SUCCESS;
+  if (a->bm > 64 || a->bk > 64) return fail(KAIRO_STATUS_NOT_SUPPORTED, "transpose supports blocks up to 64 x 64");
+  const int g = static_cast<int>(std::min<int64_t>(a->nnzb, 148 * 16));
+  switch (a->dtype) {
+    case KAIRO_DTYPE_F32:
+      k_transpose_blocks<float><<<g, 256, 0, s>>>(static_cast<const float*>(a->blocks), a->blk_idx, perm_t, a->nnzb,
+                                                  a->nblocks_stored, a->bm, a->bk, static_cast<float*>(blocks_t), err);
+      break;
+    case KAIRO_DTYPE_F16:
+      k_transpose_blocks<__half><<<g, 256, 0, s>>>(static_cast<const __half*>(a->blocks), a->blk_idx, perm_t, a->nnzb,
+                                                   a->nblocks_stored, a->bm, a->bk, static_cast<__half*>(blocks_t), err);
+      break;
+    case KAIRO_DTYPE_BF16:
+      k_transpose_blocks<__nv_bfloat16><<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(a->blocks), a->blk_idx,
+                                                          perm_t, a->nnzb, a->nblocks_stored, a->bm, a->bk,
+                                                          static_cast<__nv_bfloat16*>(blocks_t), err);
+      break;
+    default:
+      return fail(KAIRO_STATUS_INVALID_VALUE, "unknown dtype");
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch of the block transpose kernel");
+  return KAIRO_STATUS_SUCCESS;
+}
+
+kairo_status check_transpose_args(const kairo_bsr* a) {
+  if (!a) return fail(KAIRO_STATUS_INVALID_VALUE, "null BSR descriptor");
+  if (a->nbr < 0 || a->nnzb < 0 || a->bm <= 0 || a->bk <= 0 || a->rows < 0 || a->cols < 0)
+    return fail(KAIRO_STATUS_INVALID_VALUE, "invalid BSR size");
+  if (a->nnzb > 0x7fffffffLL) return fail(KAIRO_STATUS_NOT_SUPPORTED, "more than 2^31-1 blocks");
+  if (a->nbr > 0 && !a->row_ptr) return fail(KAIRO_STATUS_INVALID_VALUE, "null row_ptr");
+  if (a->nnzb > 0 && !a->col_idx) return fail(KAIRO_STATUS_INVALID_VALUE, "null col_idx");
+  return KAIRO_STATUS_SUCCESS;
+}
+
+}  // namespace
+}  // namespace kairo
+
+extern "C" kairo_status kairo_bsr_transpose_workspace_size(const kairo_bsr* a, size_t* bytes) {
+  kairo_status st = check_transpose_args(a);
+  if (st) return st;
+  if (!bytes) return fail(KAIRO_STATUS_INVALID_VALUE, "null argument");
+  *bytes = transpose_ws_bytes(a->nnzb, static_cast<int32_t>(ceil_div64(a->cols, a->bk)));
+  return KAIRO_STATUS_SUCCESS;
+}
+
+extern "C" kairo_status kairo_bsr_transpose(const kairo_bsr* a, int32_t* row_ptr_t, int32_t* col_idx_t,
+                                            int32_t* perm_t, void* blocks_t, void* workspace,
+                                            size_t workspace_bytes, void* stream) {
+  kairo_status st = check_transpose_args(a);
+  if (st) return st;
+  const int64_t nbc64 = ceil_div64(a->cols, a->bk);
+  if (nbc64 > 0x7fffffffLL) return fail(KAIRO_STATUS_NOT_SUPPORTED, "too many block-columns");
+  const int32_t nbc = static_cast<int32_t>(nbc64);
+  if (!row_ptr_t || !workspace || (a->nnzb > 0 && (!col_idx_t || !perm_t)))
+    return fail(KAIRO_STATUS_INVALID_VALUE, "null pointer argument");
+  if (blocks_t && a->nnzb > 0 && !a->blocks) return fail(KAIRO_STATUS_INVALID_VALUE, "null blocks");
+  const size_t need = transpose_ws_bytes(a->nnzb, nbc);
+  if (workspace_bytes < need) return fail(KAIRO_STATUS_WORKSPACE_TOO_SMALL, "transpose workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  TransposeWs w = carve_transpose(workspace, nbc);
+  const size_t clear = reinterpret_cast<uint8_t*>(w.rows_of_pos) - static_cast<uint8_t*>(workspace);
+  cudaError_t e = cudaMemsetAsync(workspace, 0, clear, s);
+  // flags[0] = 1: the column-major list is unsorted, so the build kernels
+  // scatter into buckets and sort each bucket by original position.
+  if (e == cudaSuccess) e = cudaMemsetAsync(w.flags, 1, 1, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(transpose workspace)");
+  const int64_t nnzb = a->nnzb;
+  if (nnzb > 0) {
+    const int rows_grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((a->nbr + 7) / 8, 148 * 32)));
+    k_expand_rows<<<rows_grid, 256, 0, s>>>(a->row_ptr, a->nbr, nnzb, w.rows_of_pos);
+    k_count<<<grid_for(nnzb, 256), 256, 0, s>>>(a->col_idx, w.rows_of_pos, nnzb, nbc, a->nbr, w.counts, w.flags,
+                                                w.err);
+  }
+  k_scan<<<1, kScanThreads, 0, s>>>(w.counts, nbc, row_ptr_t, w.flags);
+  if (nnzb > 0) {
+    k_place<<<grid_for(nnzb, 256), 256, 0, s>>>(a->col_idx, w.rows_of_pos, nnzb, row_ptr_t, w.fill, col_idx_t,
+                                                perm_t, w.flags, w.err);
+    static bool attr_set[64] = {false};
+    const int dev = current_device();
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+      e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&k_segsort), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kSortMax * static_cast<int>(sizeof(int)));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_segsort)");
+      attr_set[dev] = true;
+    }
+    k_segsort<<<std::max(1, std::min(nbc, 148 * 8)), 1024, kSortMax * sizeof(int), s>>>(
+        w.rows_of_pos, row_ptr_t, nbc, col_idx_t, perm_t, w.flags, w.err);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch of the transpose kernels");
+  if (blocks_t) return transpose_values(a, perm_t, blocks_t, w.err, s);
+  return KAIRO_STATUS_SUCCESS;
+}
+
+extern "C" kairo_status kairo_bsr_transpose_values(const kairo_bsr* a, const int32_t* perm_t, void* blocks_t,
+                                                   void* workspace, size_t workspace_bytes, void* stream) {
+  kairo_status st = check_transpose_args(a);
+  if (st) return st;
+  if (a->nnzb == 0) return KAIRO_STATUS_SUCCESS;
+  if (!perm_t || !blocks_t || !a->blocks || !workspace) return fail(KAIRO_STATUS_INVALID_VALUE, "null pointer argument");
+  if (workspace_bytes < kWorkspaceHeaderBytes) return fail(KAIRO_STATUS_WORKSPACE_TOO_SMALL, "workspace too small");
+  return transpose_values(a, perm_t, blocks_t, static_cast<unsigned*>(workspace), static_cast<cudaStream_t>(stream));
 }

@@ -8,6 +8,14 @@ plus the BSR-level operators of this package.
 from __future__ import annotations
 
 from kairo_b200.ops._autotuner import TileAutotuner, TileConfig
+from kairo_b200.ops.backward import (
+    BlockSparseLinear,
+    TransposedBsr,
+    bsr_transpose,
+    sparse_linear_backward,
+    sparse_linear_weight_grad,
+    transpose_values,
+)
 from kairo_b200.ops.spmm import (
     KernelConfig,
     block_sparse_mm,
@@ -38,6 +46,12 @@ __all__ = [
     "describe",
     "sparse_linear",
     "KernelConfig",
+    "BlockSparseLinear",
+    "TransposedBsr",
+    "bsr_transpose",
+    "sparse_linear_backward",
+    "sparse_linear_weight_grad",
+    "transpose_values",
     "TileAutotuner",
     "TileConfig",
 ]

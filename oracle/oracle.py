@@ -59,6 +59,12 @@ def load() -> ctypes.CDLL:
                 h.oracle_row_offsets.argtypes = [c_void_p, c_int64, c_int64, c_void_p]
                 h.oracle_num_threads.restype = c_int
                 h.oracle_num_threads.argtypes = []
+                h.oracle_bsr_sddmm.restype = c_int
+                h.oracle_bsr_sddmm.argtypes = [c_void_p, c_void_p, c_int32, c_int64, c_void_p, c_int64, c_void_p,
+                                               c_int64, c_int, c_int64, c_int64, c_int64, c_int32, c_int32, c_void_p,
+                                               c_int]
+                h.oracle_bsr_transpose.restype = c_int
+                h.oracle_bsr_transpose.argtypes = [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p]
                 _lib = h
     return _lib
 
@@ -144,3 +150,36 @@ def row_offsets(rows: torch.Tensor, nrows: int) -> torch.Tensor:
     out = torch.empty(nrows + 1, dtype=torch.int64)
     load().oracle_row_offsets(r.data_ptr(), r.numel(), nrows, out.data_ptr())
     return out
+
+
+def bsr_sddmm(row_ptr: torch.Tensor, col_idx: torch.Tensor, dY: torch.Tensor, X: torch.Tensor, bm: int, bk: int,
+              nthreads: int = 0) -> torch.Tensor:
+    """dW blocks (nnzb, bm, bk) fp32 of Y = X @ W.T on W's nonzero blocks."""
+    rp = _cpu(row_ptr, torch.int32)
+    ci = _cpu(col_idx, torch.int32)
+    dY = _cpu(dY)
+    X = _cpu(X)
+    if dY.dtype != X.dtype or dY.dim() != 2 or X.dim() != 2 or dY.shape[0] != X.shape[0]:
+        raise ValueError("dY and X must be 2-D, same dtype and batch rows")
+    nnzb = ci.numel()
+    dw = torch.empty(nnzb, bm, bk, dtype=torch.float32)
+    rc = load().oracle_bsr_sddmm(rp.data_ptr(), ci.data_ptr(), rp.numel() - 1, nnzb, dY.data_ptr(), dY.stride(0),
+                                 X.data_ptr(), X.stride(0), _DT[dY.dtype], dY.shape[0], dY.shape[1], X.shape[1], bm,
+                                 bk, dw.data_ptr(), nthreads)
+    if rc:
+        raise ValueError(f"oracle_bsr_sddmm failed ({rc})")
+    return dw
+
+
+def bsr_transpose(row_ptr: torch.Tensor, col_idx: torch.Tensor, nbc: int):
+    """(row_ptr_t, col_idx_t, perm_t) of W^T, int32."""
+    rp = _cpu(row_ptr, torch.int32)
+    ci = _cpu(col_idx, torch.int32)
+    rpt = torch.empty(nbc + 1, dtype=torch.int32)
+    cit = torch.empty(ci.numel(), dtype=torch.int32)
+    pt = torch.empty(ci.numel(), dtype=torch.int32)
+    rc = load().oracle_bsr_transpose(rp.data_ptr(), ci.data_ptr(), rp.numel() - 1, nbc, rpt.data_ptr(),
+                                     cit.data_ptr(), pt.data_ptr())
+    if rc:
+        raise ValueError("oracle_bsr_transpose: block-column out of range")
+    return rpt, cit, pt
