@@ -248,6 +248,25 @@ KAIRO_API kairo_status kairo_bsr_sddmm(const kairo_bsr* a, const int32_t* row_pt
 KAIRO_API kairo_status kairo_bsr_sddmm_workspace_size(const kairo_bsr* a, size_t* bytes);
 
 /* ------------------------------------------------------------------------
+ * Block-granular pruning (no counterpart in the reference, which prunes
+ * element by element: kairo/training/sparse_rec/topology.py:50-118).
+ *   kairo_block_norms      L2 norm of every bm x bk block of a dense matrix
+ *                          (m x k, lda), fp32, row-major over the block grid.
+ *   kairo_bsr_block_norms  L2 norm of every BSR block, in BSR order.
+ *   kairo_topk_indices     indices of the `count` largest scores, ascending;
+ *                          ties at the threshold go to the lower index, NaN
+ *                          ranks lowest ("topk, then sort" of the reference's
+ *                          prune_mask for distinct scores).
+ * All asynchronous on `stream`.
+ * ---------------------------------------------------------------------- */
+KAIRO_API kairo_status kairo_block_norms(const void* a, int64_t m, int64_t k, int64_t lda, int32_t bm, int32_t bk,
+                                         kairo_dtype dtype, float* norms, void* stream);
+KAIRO_API kairo_status kairo_bsr_block_norms(const kairo_bsr* a, float* norms, void* stream);
+KAIRO_API kairo_status kairo_topk_indices(const float* scores, int64_t n, int64_t count, int64_t* out,
+                                          void* workspace, size_t workspace_bytes, void* stream);
+KAIRO_API kairo_status kairo_topk_workspace_size(int64_t n, size_t* bytes);
+
+/* ------------------------------------------------------------------------
  * Dense A (M x K, leading dimension lda) -> tiles (num_tiles, tile, tile) in
  * COO order, zero-padding tiles that cross the right/bottom edge.  Replaces
  * the per-tile host loop of _dense_to_block_sparse (kairo/ops/spmm.py:16-55).
