@@ -459,6 +459,183 @@ def run_e2e(args, spec, a, b, out, cfg, dev, stream, linear, world, dist):
             "path": "pinned host -> device copies, kairo_b200.ops.block_sparse_mm_bsr, device -> pinned host"}
 
 
+# ---------------------------------------------------------------- embedding ops
+
+EMB_WORKLOADS = {
+    # the reference's embedding benchmark shape (benchmarks/bench_embedding.py:
+    # 35-46: 10000 x 64 table, batch 256, 80 % sparse mask), fp32
+    "emb_ref_bench": {"n": 10000, "d": 64, "batch": 256, "sparsity": 0.8},
+    # a production-sized table: 1M x 128 fp32 (512 MiB), batch 65536
+    "emb_large": {"n": 1_000_000, "d": 128, "batch": 65536, "sparsity": 0.8},
+}
+
+
+def emb_problem(name: str, dev, seed: int):
+    """Seeded table, element mask (each entry active with probability
+    1 - sparsity, row-major order) and a batch of uniform ids with repeats."""
+    from kairo_b200.types import SparseMask
+
+    w = EMB_WORKLOADS[name]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    n, d, b = w["n"], w["d"], w["batch"]
+    weight = torch.randn(n, d, generator=g, device=dev)
+    keep = torch.rand(n, d, generator=g, device=dev) >= w["sparsity"]
+    idx = keep.nonzero().t().contiguous()
+    del keep
+    mask = SparseMask(indices=idx, values=torch.ones(idx.shape[1], device=dev), dense_shape=(n, d),
+                      sparsity_ratio=w["sparsity"])
+    ids = torch.randint(0, n, (b,), generator=g, device=dev)
+    grad = torch.randn(b, d, generator=g, device=dev)
+    return w, weight, mask, ids, grad
+
+
+def emb_bytes(op: str, w: dict, ids, row_offsets, active) -> float:
+    """Algorithmic bytes of one launch (fp32): gather reads every id, its row
+    offsets and each active (column id, value) pair and writes the output
+    row; scatter writes the dense gradient once and reads the batch ids,
+    the gradient rows and the active ids."""
+    d, b = w["d"], w["batch"]
+    if op == "gather":
+        per_row = (row_offsets[1:] - row_offsets[:-1])[ids]
+        return float(b * (8 + 16 + 4 * d) + int(per_row.sum()) * (8 + 4))
+    return float(w["n"] * d * 4 + b * (8 + 4 * d) + active.numel() * 8)
+
+
+def run_embedding(args) -> None:
+    from kairo_b200.ops import sort_mask_rows, sparse_gather, sparse_scatter_grad
+
+    rank, world, local = dist_env()
+    if world > 1:
+        raise SystemExit("--op gather/scatter runs on one GPU (independent replicas need no collective)")
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    name = args.emb_workload
+    w, weight, mask, ids, grad = emb_problem(name, dev, args.seed)
+    mr = sort_mask_rows(mask)
+    active = torch.unique(ids)
+    n, d = w["n"], w["d"]
+    out = None
+
+    if args.op == "gather":
+        def step():
+            return sparse_gather(weight, mr, ids)
+    else:
+        def step():
+            return sparse_scatter_grad(grad, active, ids, n, d)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    sampler = ClockSampler(dev)
+    with sampler:
+        for _ in range(args.warmup):
+            flush.zero_()
+            out = step()
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            out = step()
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
+    rows_per_s = w["batch"] / (ms / 1e3)
+    nbytes = emb_bytes(args.op, w, ids, mr.row_offsets, active)
+    peaks, peak_kind = measured_peaks()
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    achieved = nbytes / (ms / 1e3) / 1e9
+
+    # End to end: ids (and the gradient rows) from pinned host memory, the
+    # result back to pinned host memory, inside the timed region.
+    h_ids = ids.cpu().pin_memory()
+    h_grad = grad.cpu().pin_memory() if args.op == "scatter" else None
+    h_active = active.cpu().pin_memory()
+    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    d_ids = torch.empty_like(ids)
+    d_grad = torch.empty_like(grad) if args.op == "scatter" else None
+    d_active = torch.empty_like(active)
+
+    def one():
+        d_ids.copy_(h_ids, non_blocking=True)
+        if args.op == "gather":
+            r = sparse_gather(weight, mr, d_ids)
+        else:
+            d_grad.copy_(h_grad, non_blocking=True)
+            d_active.copy_(h_active, non_blocking=True)
+            r = sparse_scatter_grad(d_grad, d_active, d_ids, n, d)
+        h_out.copy_(r, non_blocking=True)
+
+    one()
+    torch.cuda.synchronize()
+    e_steps = max(1, min(args.steps, args.e2e_steps))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e_steps):
+        one()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e_steps
+    h2d = h_ids.numel() * 8 + (h_grad.numel() * 4 + h_active.numel() * 8 if args.op == "scatter" else 0)
+    d2h = h_out.numel() * h_out.element_size()
+
+    cpu = None
+    if not args.no_cpu:
+        cpu = emb_cpu_sample(args.op, w, weight, mr, ids, grad, active, args.cpu_seconds)
+    line = {
+        "metric": f"embedding_{args.op}_rows_per_s",
+        "value": rows_per_s,
+        "unit": "rows/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded, generated on device)",
+        "config": {"workload": name, **w, "mask_nnz": mr.nnz, "active_rows": int(active.numel()),
+                   "parallelism": "single GPU", "l2": "flushed before every step (256 MiB write, untimed)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "traffic": None, "peak_kind": peak_kind,
+                     "bytes_definition": ("ids + row offsets + active (col, value) pairs + output rows"
+                                          if args.op == "gather" else
+                                          "dense gradient write + batch ids + gradient rows + active ids")},
+        "cpu_baseline": cpu,
+        "e2e": {"value": w["batch"] / (e2e_ms / 1e3), "unit": "rows/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": e_steps},
+        "gpu_launches": args.steps * (1 if args.op == "gather" else 7),
+        "clocks": sampler.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+def emb_cpu_sample(op, w, weight, mr, ids, grad, active, target_s: float):
+    """The oracle (one thread) on the first ids of the batch, sized for about
+    ``target_s`` seconds; rows/s."""
+    from oracle import oracle
+
+    ro = mr.row_offsets.cpu()
+    cols = mr.cols.cpu()
+    h_ids = ids.cpu()
+    if op == "gather":
+        hw = weight.cpu()
+        t0 = time.perf_counter()
+        oracle.sparse_gather(hw, ro, cols, h_ids)
+        dt = time.perf_counter() - t0
+        desc = f"all {h_ids.numel()} ids of the batch, 1 thread"
+        return {"value": h_ids.numel() / dt, "unit": "rows/s", "cores": 1, "kind": "port", "sample": desc}
+    hg = grad.cpu()
+    ha = active.cpu()
+    t0 = time.perf_counter()
+    oracle.sparse_scatter_grad(hg, ha, h_ids, w["n"], w["d"])
+    dt = time.perf_counter() - t0
+    desc = f"the whole batch ({h_ids.numel()} rows) into the {w['n']} x {w['d']} gradient, 1 thread"
+    return {"value": h_ids.numel() / dt, "unit": "rows/s", "cores": 1, "kind": "port", "sample": desc}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -479,10 +656,17 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=3.0)
+    ap.add_argument("--op", choices=("spmm", "gather", "scatter"), default="spmm",
+                    help="spmm (default): the block-sparse SpMM; gather/scatter: the masked embedding ops")
+    ap.add_argument("--emb-workload", choices=sorted(EMB_WORKLOADS), default="emb_large")
     args = ap.parse_args()
     if args.warmup < 3:
         log("warning: fewer than 3 warm-up steps")
-    if args.impl == "reference":
+    if args.op != "spmm":
+        if args.impl == "reference":
+            raise SystemExit("--impl reference times the SpMM path only")
+        run_embedding(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -267,6 +267,47 @@ KAIRO_API kairo_status kairo_topk_indices(const float* scores, int64_t n, int64_
 KAIRO_API kairo_status kairo_topk_workspace_size(int64_t n, size_t* bytes);
 
 /* ------------------------------------------------------------------------
+ * Masked embedding lookup and its gradient (the reference's other extension
+ * functions, csrc/bindings.cpp:39-82 -> csrc/sparse_embedding_kernel.cu:
+ * 135-219, called from kairo/ops/sparse_embedding.py:59-161).
+ *   kairo_coo_sort_rows   stable sort of a COO element mask by row on the
+ *                         device (_sort_coo_by_row, sparse_embedding.py:49-56)
+ *                         and its int64 row offsets (_coo_to_row_offsets,
+ *                         :23-46).  rows_sorted and perm may be NULL.  Rows of
+ *                         more than 16384 entries keep an unspecified order.
+ *                         Ids outside [0, n_rows) x [0, n_cols) set the
+ *                         workspace error word (KAIRO_DEVERR_BAD_INDEX).
+ *   kairo_sparse_gather   out[b, :] = weight[ids[b], :] on the row's active
+ *                         columns, 0 elsewhere; an id outside [0, n_rows)
+ *                         gives a zero row (sparse_gather_forward).  weight
+ *                         is (n_rows, dim) row-major, out (nids, dim); mask
+ *                         values are not read (an entry means "active").
+ *   kairo_sparse_scatter_grad
+ *                         grad_weight (n_rows, dim, written whole) = the sum
+ *                         of grad_output's rows b with batch_ids[b] == r for
+ *                         every r in active_ids (sorted, unique), 0 on all
+ *                         other rows (sparse_scatter_backward).  Sums run in
+ *                         fp32 in ascending b order: deterministic, no
+ *                         atomics.  An active id outside [0, n_rows) sets
+ *                         the workspace error word.
+ * dtype f32, f16 or bf16; all asynchronous on `stream`.
+ * ---------------------------------------------------------------------- */
+KAIRO_API kairo_status kairo_coo_sort_rows(const int64_t* rows, const int64_t* cols, int64_t nnz, int64_t n_rows,
+                                           int64_t n_cols, int64_t* row_offsets, int64_t* rows_sorted,
+                                           int64_t* cols_sorted, int64_t* perm, void* workspace,
+                                           size_t workspace_bytes, void* stream);
+KAIRO_API kairo_status kairo_coo_sort_rows_workspace_size(int64_t n_rows, int64_t nnz, size_t* bytes);
+KAIRO_API kairo_status kairo_sparse_gather(const void* weight, int64_t n_rows, int64_t dim, kairo_dtype dtype,
+                                           const int64_t* row_offsets, const int64_t* mask_cols, int64_t nnz,
+                                           const int64_t* ids, int64_t nids, void* out, void* stream);
+KAIRO_API kairo_status kairo_sparse_scatter_grad(const void* grad_output, kairo_dtype dtype,
+                                                 const int64_t* active_ids, int64_t nactive,
+                                                 const int64_t* batch_ids, int64_t nbatch, int64_t n_rows,
+                                                 int64_t dim, void* grad_weight, void* workspace,
+                                                 size_t workspace_bytes, void* stream);
+KAIRO_API kairo_status kairo_sparse_scatter_grad_workspace_size(int64_t nactive, int64_t nbatch, size_t* bytes);
+
+/* ------------------------------------------------------------------------
  * Dense A (M x K, leading dimension lda) -> tiles (num_tiles, tile, tile) in
  * COO order, zero-padding tiles that cross the right/bottom edge.  Replaces
  * the per-tile host loop of _dense_to_block_sparse (kairo/ops/spmm.py:16-55).

@@ -155,6 +155,14 @@ _SIGNATURES = {
     "kairo_bsr_block_norms": (c_int32, [POINTER(KairoBsr), c_void_p, c_void_p]),
     "kairo_topk_indices": (c_int32, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_size_t, c_void_p]),
     "kairo_topk_workspace_size": (c_int32, [c_int64, POINTER(c_size_t)]),
+    "kairo_coo_sort_rows": (c_int32, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                                      c_void_p, c_void_p, c_size_t, c_void_p]),
+    "kairo_coo_sort_rows_workspace_size": (c_int32, [c_int64, c_int64, POINTER(c_size_t)]),
+    "kairo_sparse_gather": (c_int32, [c_void_p, c_int64, c_int64, c_int32, c_void_p, c_void_p, c_int64, c_void_p,
+                                      c_int64, c_void_p, c_void_p]),
+    "kairo_sparse_scatter_grad": (c_int32, [c_void_p, c_int32, c_void_p, c_int64, c_void_p, c_int64, c_int64,
+                                            c_int64, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "kairo_sparse_scatter_grad_workspace_size": (c_int32, [c_int64, c_int64, POINTER(c_size_t)]),
     "kairo_dense_to_tiles": (c_int32, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int32,
                                        c_int32, c_void_p, c_void_p]),
     "kairo_acc_spmm_forward": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,

@@ -17,7 +17,7 @@
 namespace kairo {
 namespace {
 
-constexpr int kSortMax = 16384;  // longest unsorted block-row sorted in shared memory
+constexpr int kSortMax = kBucketSortMax;  // longest unsorted block-row sorted in shared memory
 constexpr int kScanThreads = 1024;
 
 // Build-workspace layout (after the 256-byte header holding the error word):
@@ -123,7 +123,8 @@ __global__ void k_place(const int32_t* __restrict__ rows, const int32_t* __restr
 // in shared memory, then col_idx from the sorted indices.
 __global__ void __launch_bounds__(1024) k_segsort(const int32_t* __restrict__ cols, const int32_t* __restrict__ row_ptr,
                                                   int32_t nbr, int32_t* __restrict__ col_idx,
-                                                  int32_t* __restrict__ perm, const int* flags, unsigned* err) {
+                                                  int32_t* __restrict__ perm, const int* flags, unsigned* err,
+                                                  bool long_rows_ok = false) {
   if (flags[0] == 0 || *err) return;
   extern __shared__ int keys[];
   for (int r = blockIdx.x; r < nbr; r += gridDim.x) {
@@ -131,7 +132,8 @@ __global__ void __launch_bounds__(1024) k_segsort(const int32_t* __restrict__ co
     const int len = p1 - p0;
     if (len == 0) continue;
     if (len > kSortMax) {
-      if (threadIdx.x == 0) atomicCAS(err, 0u, KAIRO_DEVERR_ROW_TOO_LONG);
+      // Left unsorted; a caller that allows it orders such buckets itself.
+      if (threadIdx.x == 0 && !long_rows_ok) atomicCAS(err, 0u, KAIRO_DEVERR_ROW_TOO_LONG);
       continue;
     }
     int pw = 1;
@@ -348,36 +350,60 @@ extern "C" kairo_status kairo_dense_to_tiles(const void* a, int64_t m, int64_t k
   return KAIRO_STATUS_SUCCESS;
 }
 
+// ------------------------------------------------------------ bucket sort
+
+namespace kairo {
+
+// Bucket-sort workspace: header (error word, flags), per-bucket counts and
+// fill counters.
+size_t bucket_sort_ws_bytes(int32_t nbuckets) {
+  return kWorkspaceHeaderBytes + 2 * align_up(static_cast<size_t>(nbuckets), 64) * sizeof(int);
+}
+
+kairo_status bucket_sort(const int32_t* keys, const int32_t* vals, int32_t nvals, int64_t n, int32_t nbuckets,
+                         int32_t* bucket_ptr, int32_t* perm, int32_t* vals_sorted, void* ws, cudaStream_t s,
+                         bool long_buckets_ok) {
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  unsigned* err = reinterpret_cast<unsigned*>(p);
+  int* flags = reinterpret_cast<int*>(p + 64);
+  int* counts = reinterpret_cast<int*>(p + kWorkspaceHeaderBytes);
+  int* fill = counts + align_up(static_cast<size_t>(nbuckets), 64);
+  cudaError_t e = cudaMemsetAsync(ws, 0, bucket_sort_ws_bytes(nbuckets), s);
+  // flags[0] = 1: the key list is treated as unsorted, so every bucket is
+  // filled by atomic scatter and then sorted by original index.
+  if (e == cudaSuccess) e = cudaMemsetAsync(flags, 1, 1, s);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(bucket-sort workspace)");
+  if (n > 0) k_count<<<grid_for(n, 256), 256, 0, s>>>(keys, vals, n, nbuckets, nvals, counts, flags, err);
+  k_scan<<<1, kScanThreads, 0, s>>>(counts, nbuckets, bucket_ptr, flags);
+  if (n > 0) {
+    k_place<<<grid_for(n, 256), 256, 0, s>>>(keys, vals, n, bucket_ptr, fill, vals_sorted, perm, flags, err);
+    static bool attr_set[64] = {false};
+    const int dev = current_device();
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+      e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&k_segsort), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kSortMax * static_cast<int>(sizeof(int)));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_segsort)");
+      attr_set[dev] = true;
+    }
+    k_segsort<<<std::max(1, std::min(nbuckets, 148 * 8)), 1024, kSortMax * sizeof(int), s>>>(
+        vals, bucket_ptr, nbuckets, vals_sorted, perm, flags, err, long_buckets_ok);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch of the bucket-sort kernels");
+  return KAIRO_STATUS_SUCCESS;
+}
+
+}  // namespace kairo
+
 // ------------------------------------------------------------ transpose
 
 namespace kairo {
 namespace {
 
-// Transpose workspace: header (error word, flags), per-column counts and
-// fill counters, then the block-row of every BSR position.
-struct TransposeWs {
-  unsigned* err;
-  int* flags;
-  int* counts;
-  int* fill;
-  int32_t* rows_of_pos;
-};
-
+// Transpose workspace: the bucket sort's, then the block-row of every BSR
+// position.
 size_t transpose_ws_bytes(int64_t nnzb, int32_t nbc) {
-  const size_t col = align_up(static_cast<size_t>(nbc), 64) * sizeof(int);
-  return kWorkspaceHeaderBytes + 2 * col + align_up(static_cast<size_t>(nnzb), 64) * sizeof(int32_t);
-}
-
-TransposeWs carve_transpose(void* ws, int32_t nbc) {
-  uint8_t* p = static_cast<uint8_t*>(ws);
-  TransposeWs w;
-  w.err = reinterpret_cast<unsigned*>(p);
-  w.flags = reinterpret_cast<int*>(p + 64);
-  const size_t col = align_up(static_cast<size_t>(nbc), 64);
-  w.counts = reinterpret_cast<int*>(p + kWorkspaceHeaderBytes);
-  w.fill = w.counts + col;
-  w.rows_of_pos = w.fill + col;
-  return w;
+  return bucket_sort_ws_bytes(nbc) + align_up(static_cast<size_t>(nnzb), 64) * sizeof(int32_t);
 }
 
 kairo_status transpose_values(const kairo_bsr* a, const int32_t* perm_t, void* blocks_t, unsigned* err,
@@ -439,41 +465,19 @@ extern "C" kairo_status kairo_bsr_transpose(const kairo_bsr* a, int32_t* row_ptr
   if (!row_ptr_t || !workspace || (a->nnzb > 0 && (!col_idx_t || !perm_t)))
     return fail(KAIRO_STATUS_INVALID_VALUE, "null pointer argument");
   if (blocks_t && a->nnzb > 0 && !a->blocks) return fail(KAIRO_STATUS_INVALID_VALUE, "null blocks");
-  const size_t need = transpose_ws_bytes(a->nnzb, nbc);
-  if (workspace_bytes < need) return fail(KAIRO_STATUS_WORKSPACE_TOO_SMALL, "transpose workspace too small");
+  if (workspace_bytes < transpose_ws_bytes(a->nnzb, nbc))
+    return fail(KAIRO_STATUS_WORKSPACE_TOO_SMALL, "transpose workspace too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  TransposeWs w = carve_transpose(workspace, nbc);
-  const size_t clear = reinterpret_cast<uint8_t*>(w.rows_of_pos) - static_cast<uint8_t*>(workspace);
-  cudaError_t e = cudaMemsetAsync(workspace, 0, clear, s);
-  // flags[0] = 1: the column-major list is unsorted, so the build kernels
-  // scatter into buckets and sort each bucket by original position.
-  if (e == cudaSuccess) e = cudaMemsetAsync(w.flags, 1, 1, s);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(transpose workspace)");
-  const int64_t nnzb = a->nnzb;
-  if (nnzb > 0) {
+  // W^T order = W's positions bucketed by block-column, stable: the bucket
+  // sort of keys col_idx[p], carrying each position's block-row.
+  int32_t* rows_of_pos = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + bucket_sort_ws_bytes(nbc));
+  if (a->nnzb > 0) {
     const int rows_grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((a->nbr + 7) / 8, 148 * 32)));
-    k_expand_rows<<<rows_grid, 256, 0, s>>>(a->row_ptr, a->nbr, nnzb, w.rows_of_pos);
-    k_count<<<grid_for(nnzb, 256), 256, 0, s>>>(a->col_idx, w.rows_of_pos, nnzb, nbc, a->nbr, w.counts, w.flags,
-                                                w.err);
+    k_expand_rows<<<rows_grid, 256, 0, s>>>(a->row_ptr, a->nbr, a->nnzb, rows_of_pos);
   }
-  k_scan<<<1, kScanThreads, 0, s>>>(w.counts, nbc, row_ptr_t, w.flags);
-  if (nnzb > 0) {
-    k_place<<<grid_for(nnzb, 256), 256, 0, s>>>(a->col_idx, w.rows_of_pos, nnzb, row_ptr_t, w.fill, col_idx_t,
-                                                perm_t, w.flags, w.err);
-    static bool attr_set[64] = {false};
-    const int dev = current_device();
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-      e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&k_segsort), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kSortMax * static_cast<int>(sizeof(int)));
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_segsort)");
-      attr_set[dev] = true;
-    }
-    k_segsort<<<std::max(1, std::min(nbc, 148 * 8)), 1024, kSortMax * sizeof(int), s>>>(
-        w.rows_of_pos, row_ptr_t, nbc, col_idx_t, perm_t, w.flags, w.err);
-  }
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "launch of the transpose kernels");
-  if (blocks_t) return transpose_values(a, perm_t, blocks_t, w.err, s);
+  st = bucket_sort(a->col_idx, rows_of_pos, a->nbr, a->nnzb, nbc, row_ptr_t, perm_t, col_idx_t, workspace, s);
+  if (st) return st;
+  if (blocks_t) return transpose_values(a, perm_t, blocks_t, static_cast<unsigned*>(workspace), s);
   return KAIRO_STATUS_SUCCESS;
 }
 

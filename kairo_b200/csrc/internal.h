@@ -131,4 +131,19 @@ kairo_status simt_launch(const kairo_bsr* a, const void* b, int64_t ldb, int64_t
 // BSR construction (bsr_build.cu)
 size_t bsr_build_ws_bytes(int64_t num_tiles, int32_t nbr);
 
+// Stable bucket sort on the device, asynchronously (bsr_build.cu).  For t in
+// [0, n): keys[t] in [0, nbuckets), vals[t] in [0, nvals) (anything else is
+// recorded as KAIRO_DEVERR_BAD_INDEX in the workspace error word).  Writes
+// bucket_ptr (nbuckets + 1 offsets), perm (the original index of every
+// sorted position, ascending inside a bucket) and vals_sorted[q] =
+// vals[perm[q]].  A bucket of more than kBucketSortMax entries is left in
+// arbitrary order and records KAIRO_DEVERR_ROW_TOO_LONG unless
+// long_buckets_ok.  ws needs bucket_sort_ws_bytes(nbuckets) bytes and starts
+// with the error word.
+constexpr int kBucketSortMax = 16384;
+size_t bucket_sort_ws_bytes(int32_t nbuckets);
+kairo_status bucket_sort(const int32_t* keys, const int32_t* vals, int32_t nvals, int64_t n, int32_t nbuckets,
+                         int32_t* bucket_ptr, int32_t* perm, int32_t* vals_sorted, void* ws, cudaStream_t s,
+                         bool long_buckets_ok = false);
+
 }  // namespace kairo

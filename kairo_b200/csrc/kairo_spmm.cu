@@ -369,7 +369,6 @@ kairo_status kairo_acc_spmm_forward(const void* a_tiles, const int32_t* tile_row
     return fail(KAIRO_STATUS_INVALID_VALUE, "null tile arrays");
   if (!workspace) return fail(KAIRO_STATUS_INVALID_VALUE, "null workspace");
   if (workspace_bytes < L.total) return fail(KAIRO_STATUS_WORKSPACE_TOO_SMALL, "acc_spmm_forward workspace too small");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int32_t* row_ptr = reinterpret_cast<int32_t*>(ws + L.row_ptr_off);
   int32_t* col_idx = reinterpret_cast<int32_t*>(ws + L.col_idx_off);
@@ -393,7 +392,6 @@ kairo_status kairo_acc_spmm_forward(const void* a_tiles, const int32_t* tile_row
   a.blk_idx = identity ? nullptr : perm;
   a.blocks = a_tiles;
   a.dtype = dtype;
-  (void)s;
   return kairo_bsr_spmm(&a, b, n, KAIRO_LAYOUT_STANDARD, n, c, n, KAIRO_DTYPE_F32, nullptr, ws + L.spmm_off,
                         L.row_ptr_off - L.spmm_off, stream);
 }

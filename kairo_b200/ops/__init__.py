@@ -1,13 +1,15 @@
 """kairo_b200.ops: the block-sparse SpMM operators (CUDA only).
 
-Mirrors the SpMM part of the reference's ``kairo.ops`` export surface
-(kairo/ops/__init__.py:5-17): ``block_sparse_mm`` and ``cuda_ext_available``,
-plus the BSR-level operators of this package.
+Mirrors the reference's ``kairo.ops`` export surface (kairo/ops/
+__init__.py:5-17): ``block_sparse_mm``, ``sparse_gather``,
+``sparse_scatter_grad`` and ``cuda_ext_available``, plus the BSR-level
+operators of this package.
 """
 
 from __future__ import annotations
 
 from kairo_b200.ops._autotuner import TileAutotuner, TileConfig
+from kairo_b200.ops.embedding import MaskRows, sort_mask_rows, sparse_gather, sparse_scatter_grad
 from kairo_b200.ops.backward import (
     BlockSparseLinear,
     TransposedBsr,
@@ -54,4 +56,8 @@ __all__ = [
     "transpose_values",
     "TileAutotuner",
     "TileConfig",
+    "MaskRows",
+    "sort_mask_rows",
+    "sparse_gather",
+    "sparse_scatter_grad",
 ]

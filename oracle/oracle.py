@@ -6,6 +6,8 @@ Restates the reference's CPU path for the SpMM hot path:
   dense_to_tiles  kairo/ops/spmm.py:16-55     (_dense_to_block_sparse)
   sort_coo_by_row kairo/ops/sparse_embedding.py:49-56
   row_offsets     kairo/ops/sparse_embedding.py:23-46
+  sparse_gather   kairo/ops/sparse_embedding.py:59-101 (the CUDA kernels' values)
+  sparse_scatter_grad kairo/ops/sparse_embedding.py:104-161
 Pinned against fixtures generated from the reference itself (tests/golden).
 Inputs are CPU torch tensors; fp16/bf16 values are widened to fp32 exactly.
 """
@@ -63,6 +65,12 @@ def load() -> ctypes.CDLL:
                 h.oracle_bsr_sddmm.argtypes = [c_void_p, c_void_p, c_int32, c_int64, c_void_p, c_int64, c_void_p,
                                                c_int64, c_int, c_int64, c_int64, c_int64, c_int32, c_int32, c_void_p,
                                                c_int]
+                h.oracle_sparse_gather.restype = None
+                h.oracle_sparse_gather.argtypes = [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                                                   c_int64, c_void_p]
+                h.oracle_sparse_scatter_grad.restype = c_int
+                h.oracle_sparse_scatter_grad.argtypes = [c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64,
+                                                         c_int64, c_int64, c_void_p]
                 h.oracle_bsr_transpose.restype = c_int
                 h.oracle_bsr_transpose.argtypes = [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p]
                 _lib = h
@@ -183,3 +191,37 @@ def bsr_transpose(row_ptr: torch.Tensor, col_idx: torch.Tensor, nbc: int):
     if rc:
         raise ValueError("oracle_bsr_transpose: block-column out of range")
     return rpt, cit, pt
+
+
+def sparse_gather(weight: torch.Tensor, row_offsets: torch.Tensor, mask_cols: torch.Tensor,
+                  ids: torch.Tensor) -> torch.Tensor:
+    """(len(ids), D) rows of weight on the row's active columns, 0 elsewhere
+    and for ids outside [0, N); weight's dtype, bit-exact copies."""
+    w = _cpu(weight)
+    ro = _cpu(row_offsets, torch.int64)
+    mc = _cpu(mask_cols, torch.int64)
+    i = _cpu(ids, torch.int64)
+    n, d = w.shape
+    if ro.numel() < n + 1:
+        raise ValueError("row_offsets must hold N + 1 entries")
+    out = torch.empty(i.numel(), d, dtype=w.dtype)
+    load().oracle_sparse_gather(w.data_ptr(), _DT[w.dtype], n, d, ro.data_ptr(), mc.data_ptr(), i.data_ptr(),
+                                i.numel(), out.data_ptr())
+    return out
+
+
+def sparse_scatter_grad(grad_output: torch.Tensor, active_ids: torch.Tensor, batch_ids: torch.Tensor,
+                        num_embeddings: int, embedding_dim: int) -> torch.Tensor:
+    """(N, D) fp32 gradient: active rows hold the batch-ordered fp32 sum of
+    their grad_output rows, every other row is 0."""
+    g = _cpu(grad_output)
+    a = _cpu(active_ids, torch.int64)
+    b = _cpu(batch_ids, torch.int64)
+    if g.numel() != b.numel() * embedding_dim:
+        raise ValueError("grad_output must be (B, D)")
+    out = torch.empty(num_embeddings, embedding_dim, dtype=torch.float32)
+    rc = load().oracle_sparse_scatter_grad(g.data_ptr(), _DT[g.dtype], a.data_ptr(), a.numel(), b.data_ptr(),
+                                           b.numel(), num_embeddings, embedding_dim, out.data_ptr())
+    if rc:
+        raise ValueError(f"oracle_sparse_scatter_grad failed ({rc})")
+    return out
