@@ -489,15 +489,14 @@ def emb_problem(name: str, dev, seed: int):
     return w, weight, mask, ids, grad
 
 
-def emb_bytes(op: str, w: dict, ids, row_offsets, active) -> float:
-    """Algorithmic bytes of one launch (fp32): gather reads every id, its row
-    offsets and each active (column id, value) pair and writes the output
-    row; scatter writes the dense gradient once and reads the batch ids,
-    the gradient rows and the active ids."""
+def emb_bytes(op: str, w: dict, ids, active) -> float:
+    """Algorithmic bytes of one launch (fp32): gather reads every id, its
+    row's mask bits (D / 8 bytes) and weight row, and writes the output row;
+    scatter writes the dense gradient once and reads the batch ids, the
+    gradient rows and the active ids."""
     d, b = w["d"], w["batch"]
     if op == "gather":
-        per_row = (row_offsets[1:] - row_offsets[:-1])[ids]
-        return float(b * (8 + 16 + 4 * d) + int(per_row.sum()) * (8 + 4))
+        return float(b * (8 + (d + 31) // 32 * 4 + 2 * 4 * d))
     return float(w["n"] * d * 4 + b * (8 + 4 * d) + active.numel() * 8)
 
 
@@ -542,7 +541,23 @@ def run_embedding(args) -> None:
         torch.cuda.synchronize()
     ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / args.steps
     rows_per_s = w["batch"] / (ms / 1e3)
-    nbytes = emb_bytes(args.op, w, ids, mr.row_offsets, active)
+    # Reference point: a device-to-device copy of the result's bytes, timed
+    # the same way (flush, events), shows what a transfer of this size reaches.
+    src = weight.reshape(-1)[: out.numel()]
+    dst = torch.empty_like(src)
+    copy_ms = []
+    for i in range(args.warmup + args.steps):
+        flush.zero_()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        dst.copy_(src)
+        c1.record(stream)
+        torch.cuda.synchronize()
+        if i >= args.warmup:
+            copy_ms.append(c0.elapsed_time(c1))
+    copy_gbs = 2 * src.numel() * 4 / (statistics.median(copy_ms) / 1e3) / 1e9
+    del dst
+    nbytes = emb_bytes(args.op, w, ids, active)
     peaks, peak_kind = measured_peaks()
     hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
     achieved = nbytes / (ms / 1e3) / 1e9
@@ -600,13 +615,16 @@ def run_embedding(args) -> None:
                    "parallelism": "single GPU", "l2": "flushed before every step (256 MiB write, untimed)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "traffic": None, "peak_kind": peak_kind,
-                     "bytes_definition": ("ids + row offsets + active (col, value) pairs + output rows"
+                     "copy_same_size_gbs": copy_gbs,
+                     "bytes_definition": ("ids + row mask bits + weight rows + output rows"
                                           if args.op == "gather" else
                                           "dense gradient write + batch ids + gradient rows + active ids")},
         "cpu_baseline": cpu,
         "e2e": {"value": w["batch"] / (e2e_ms / 1e3), "unit": "rows/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": e_steps},
-        "gpu_launches": args.steps * (1 if args.op == "gather" else 7),
+        # scatter: keys, count, scan (one CTA, or three kernels above 16384
+        # buckets), place, segment sort, sums
+        "gpu_launches": args.steps * (1 if args.op == "gather" else (6 if active.numel() + 1 <= 16384 else 8)),
         "clocks": sampler.summary(),
     }
     print(json.dumps(line), flush=True)

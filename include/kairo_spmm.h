@@ -300,6 +300,16 @@ KAIRO_API kairo_status kairo_coo_sort_rows_workspace_size(int64_t n_rows, int64_
 KAIRO_API kairo_status kairo_sparse_gather(const void* weight, int64_t n_rows, int64_t dim, kairo_dtype dtype,
                                            const int64_t* row_offsets, const int64_t* mask_cols, int64_t nnz,
                                            const int64_t* ids, int64_t nids, void* out, void* stream);
+/* Row bitmask of a COO element mask: bits is (n_rows, ceil(n_cols / 32))
+ * uint32 words, bit c % 32 of word c / 32 of row r set for entry (r, c);
+ * entries outside the grid are skipped.  kairo_sparse_gather_bits is
+ * kairo_sparse_gather reading that bitmask instead of the row offsets and
+ * columns (same result; whole rows are read with 16-byte vectors). */
+KAIRO_API kairo_status kairo_mask_bits(const int64_t* rows, const int64_t* cols, int64_t nnz, int64_t n_rows,
+                                       int64_t n_cols, uint32_t* bits, void* stream);
+KAIRO_API kairo_status kairo_sparse_gather_bits(const void* weight, int64_t n_rows, int64_t dim, kairo_dtype dtype,
+                                                const uint32_t* bits, const int64_t* ids, int64_t nids, void* out,
+                                                void* stream);
 KAIRO_API kairo_status kairo_sparse_scatter_grad(const void* grad_output, kairo_dtype dtype,
                                                  const int64_t* active_ids, int64_t nactive,
                                                  const int64_t* batch_ids, int64_t nbatch, int64_t n_rows,

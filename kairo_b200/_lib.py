@@ -160,6 +160,9 @@ _SIGNATURES = {
     "kairo_coo_sort_rows_workspace_size": (c_int32, [c_int64, c_int64, POINTER(c_size_t)]),
     "kairo_sparse_gather": (c_int32, [c_void_p, c_int64, c_int64, c_int32, c_void_p, c_void_p, c_int64, c_void_p,
                                       c_int64, c_void_p, c_void_p]),
+    "kairo_mask_bits": (c_int32, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
+    "kairo_sparse_gather_bits": (c_int32, [c_void_p, c_int64, c_int64, c_int32, c_void_p, c_void_p, c_int64,
+                                           c_void_p, c_void_p]),
     "kairo_sparse_scatter_grad": (c_int32, [c_void_p, c_int32, c_void_p, c_int64, c_void_p, c_int64, c_int64,
                                             c_int64, c_void_p, c_void_p, c_size_t, c_void_p]),
     "kairo_sparse_scatter_grad_workspace_size": (c_int32, [c_int64, c_int64, POINTER(c_size_t)]),

@@ -19,6 +19,10 @@ namespace {
 
 constexpr int kSortMax = kBucketSortMax;  // longest unsorted block-row sorted in shared memory
 constexpr int kScanThreads = 1024;
+constexpr int kScanTile = 4 * kScanThreads;  // counts per CTA of the multi-CTA scan
+constexpr int kScanSingleMax = 16384;        // up to this many buckets the scan is one CTA
+constexpr int kSegThreads = 1024;            // threads of the per-bucket sort
+constexpr int kLaneSortMax = 8;              // buckets up to this long are sorted by one thread
 
 // Build-workspace layout (after the 256-byte header holding the error word):
 //   flags[0] = row list not sorted, flags[1] = longest row
@@ -41,6 +45,9 @@ BuildWs carve(void* ws, int32_t nbr) {
 
 __global__ void k_count(const int32_t* __restrict__ rows, const int32_t* __restrict__ cols, int64_t nt, int32_t nbr,
                         int32_t nbc, int* counts, int* flags, unsigned* err) {
+  __shared__ int descending;  // this CTA saw a row id below its predecessor
+  if (threadIdx.x == 0) descending = 0;
+  __syncthreads();
   for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < nt;
        t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int r = rows[t];
@@ -50,8 +57,10 @@ __global__ void k_count(const int32_t* __restrict__ rows, const int32_t* __restr
       continue;
     }
     atomicAdd(counts + r, 1);
-    if (t > 0 && rows[t - 1] > r) flags[0] = 1;
+    if (t > 0 && rows[t - 1] > r) descending = 1;
   }
+  __syncthreads();
+  if (threadIdx.x == 0 && descending) flags[0] = 1;  // one store per CTA, not per element
 }
 
 // Exclusive scan of counts into row_ptr (nbr + 1 entries) by one CTA, in
@@ -96,7 +105,77 @@ __global__ void __launch_bounds__(kScanThreads) k_scan(const int* __restrict__ c
   if (threadIdx.x == 0) row_ptr[nbr] = carry_s;
   // longest row
   for (int o = 16; o > 0; o >>= 1) longest = max(longest, __shfl_xor_sync(0xffffffffu, longest, o));
-  if ((threadIdx.x & 31) == 0) atomicMax(flags + 1, longest);
+  if (flags && (threadIdx.x & 31) == 0) atomicMax(flags + 1, longest);
+}
+
+// Multi-CTA scan for many buckets: per-tile sums (and the longest count),
+// one-CTA scan of the tile sums, then every tile scanned with its offset.
+__global__ void __launch_bounds__(kScanThreads) k_tile_sums(const int* __restrict__ counts, int32_t n,
+                                                            int* __restrict__ tile_sum, int* flags) {
+  __shared__ int warp_sums[kScanThreads / 32];
+  const int64_t base = static_cast<int64_t>(blockIdx.x) * kScanTile;
+  const int64_t end = min(static_cast<int64_t>(n), base + kScanTile);
+  int sum = 0, longest = 0;
+  for (int64_t i = base + threadIdx.x; i < end; i += kScanThreads) {
+    const int v = counts[i];
+    sum += v;
+    longest = max(longest, v);
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    longest = max(longest, __shfl_xor_sync(0xffffffffu, longest, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    warp_sums[threadIdx.x >> 5] = sum;
+    if (flags) atomicMax(flags + 1, longest);
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    int t = warp_sums[threadIdx.x];
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) tile_sum[blockIdx.x] = t;
+  }
+}
+
+__global__ void __launch_bounds__(kScanThreads) k_scan_apply(const int* __restrict__ counts, int32_t n,
+                                                             const int* __restrict__ tile_off,
+                                                             int32_t* __restrict__ out) {
+  static_assert(kScanTile == 4 * kScanThreads, "four counts per thread");
+  __shared__ int warp_sums[kScanThreads / 32];
+  const int64_t i0 = static_cast<int64_t>(blockIdx.x) * kScanTile + 4 * threadIdx.x;
+  int v[4];
+  int t = 0;
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    v[u] = i0 + u < n ? counts[i0 + u] : 0;
+    t += v[u];
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = t;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = warp_sums[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    warp_sums[lane] = w;
+  }
+  __syncthreads();
+  int excl = x - t + (warp > 0 ? warp_sums[warp - 1] : 0) + tile_off[blockIdx.x];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    if (i0 + u < n) out[i0 + u] = excl;
+    excl += v[u];
+  }
+  if (blockIdx.x == gridDim.x - 1 && threadIdx.x == 0) out[n] = tile_off[gridDim.x];
 }
 
 // Sorted input: identity permutation.  Unsorted input: scatter every tile
@@ -119,48 +198,125 @@ __global__ void k_place(const int32_t* __restrict__ rows, const int32_t* __restr
   }
 }
 
-// One CTA per block-row: bitonic sort of the row's tile indices (ascending)
-// in shared memory, then col_idx from the sorted indices.
-__global__ void __launch_bounds__(1024) k_segsort(const int32_t* __restrict__ cols, const int32_t* __restrict__ row_ptr,
-                                                  int32_t nbr, int32_t* __restrict__ col_idx,
-                                                  int32_t* __restrict__ perm, const int* flags, unsigned* err,
-                                                  bool long_rows_ok = false) {
+// Ascending sort of one value per lane across a warp (bitonic network).
+__device__ __forceinline__ int warp_sort_asc(int v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      const int o = __shfl_xor_sync(0xffffffffu, v, j);
+      const bool up = (lane & k) == 0;
+      const bool lower = (lane & j) == 0;
+      v = (lower == up) ? min(v, o) : max(v, o);
+    }
+  }
+  return v;
+}
+
+// Sorts every unsorted bucket's tile indices (ascending, i.e. stable order)
+// and writes col_idx from them.  Each CTA takes `chunk` consecutive buckets
+// at a time, one per thread: buckets of up to kLaneSortMax entries are
+// sorted by their thread, up to 32 by a warp in registers, longer ones (up
+// to kSortMax) by the whole CTA in shared memory.
+__global__ void __launch_bounds__(kSegThreads) k_segsort(const int32_t* __restrict__ cols,
+                                                         const int32_t* __restrict__ row_ptr, int32_t nbr, int chunk,
+                                                         int32_t* __restrict__ col_idx, int32_t* __restrict__ perm,
+                                                         const int* flags, unsigned* err, bool long_rows_ok) {
   if (flags[0] == 0 || *err) return;
   extern __shared__ int keys[];
-  for (int r = blockIdx.x; r < nbr; r += gridDim.x) {
-    const int p0 = row_ptr[r], p1 = row_ptr[r + 1];
-    const int len = p1 - p0;
-    if (len == 0) continue;
-    if (len > kSortMax) {
-      // Left unsorted; a caller that allows it orders such buckets itself.
-      if (threadIdx.x == 0 && !long_rows_ok) atomicCAS(err, 0u, KAIRO_DEVERR_ROW_TOO_LONG);
-      continue;
+  __shared__ int big[kSegThreads];
+  __shared__ int nbig;
+  const int lane = threadIdx.x & 31;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * chunk; base < nbr;
+       base += static_cast<int64_t>(gridDim.x) * chunk) {
+    const int64_t r = base + threadIdx.x;
+    int p0 = 0, len = 0;
+    if (static_cast<int>(threadIdx.x) < chunk && r < nbr) {
+      p0 = row_ptr[r];
+      len = row_ptr[r + 1] - p0;
     }
-    int pw = 1;
-    while (pw < len) pw <<= 1;
+    if (threadIdx.x == 0) nbig = 0;
     __syncthreads();
-    for (int e = threadIdx.x; e < pw; e += blockDim.x) keys[e] = e < len ? perm[p0 + e] : 0x7fffffff;
-    __syncthreads();
-    for (int k = 2; k <= pw; k <<= 1) {
-      for (int j = k >> 1; j > 0; j >>= 1) {
-        for (int e = threadIdx.x; e < pw; e += blockDim.x) {
-          const int l = e ^ j;
-          if (l > e) {
-            const int a = keys[e], b = keys[l];
-            const bool up = (e & k) == 0;
-            if ((a > b) == up) {
-              keys[e] = b;
-              keys[l] = a;
-            }
-          }
-        }
-        __syncthreads();
+    if (len > 32) {
+      if (len <= kSortMax) {
+        big[atomicAdd(&nbig, 1)] = static_cast<int>(r);
+      } else if (!long_rows_ok) {
+        // Left unsorted; a caller that allows it orders such buckets itself.
+        atomicCAS(err, 0u, KAIRO_DEVERR_ROW_TOO_LONG);
       }
     }
-    for (int e = threadIdx.x; e < len; e += blockDim.x) {
-      const int t = keys[e];
-      perm[p0 + e] = t;
-      col_idx[p0 + e] = cols[t];
+    if (len > 0 && len <= kLaneSortMax) {
+      // Short bucket: sorted by its own lane in registers (odd-even
+      // transposition network over kLaneSortMax slots).
+      int a[kLaneSortMax];
+#pragma unroll
+      for (int i = 0; i < kLaneSortMax; ++i) a[i] = i < len ? perm[p0 + i] : 0x7fffffff;
+      if (len > 1) {
+#pragma unroll
+        for (int round = 0; round < kLaneSortMax; ++round) {
+#pragma unroll
+          for (int i = round & 1; i + 1 < kLaneSortMax; i += 2) {
+            const int lo = min(a[i], a[i + 1]);
+            const int hi = max(a[i], a[i + 1]);
+            a[i] = lo;
+            a[i + 1] = hi;
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kLaneSortMax; ++i) {
+        if (i < len) {
+          perm[p0 + i] = a[i];
+          col_idx[p0 + i] = cols[a[i]];
+        }
+      }
+    }
+    unsigned todo = __ballot_sync(0xffffffffu, len > kLaneSortMax && len <= 32);
+    while (todo) {
+      const int j = __ffs(todo) - 1;
+      todo &= todo - 1;
+      const int q0 = __shfl_sync(0xffffffffu, p0, j);
+      const int n = __shfl_sync(0xffffffffu, len, j);
+      int v = lane < n ? perm[q0 + lane] : 0x7fffffff;
+      v = warp_sort_asc(v);
+      if (lane < n) {
+        perm[q0 + lane] = v;
+        col_idx[q0 + lane] = cols[v];
+      }
+    }
+    __syncthreads();
+    const int nb = nbig;
+    for (int i = 0; i < nb; ++i) {
+      const int rr = big[i];
+      const int q0 = row_ptr[rr];
+      const int n = row_ptr[rr + 1] - q0;
+      int pw = 64;
+      while (pw < n) pw <<= 1;
+      for (int e = threadIdx.x; e < pw; e += kSegThreads) keys[e] = e < n ? perm[q0 + e] : 0x7fffffff;
+      __syncthreads();
+      for (int k = 2; k <= pw; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+          for (int e = threadIdx.x; e < pw; e += kSegThreads) {
+            const int l = e ^ j;
+            if (l > e) {
+              const int a = keys[e], b = keys[l];
+              const bool up = (e & k) == 0;
+              if ((a > b) == up) {
+                keys[e] = b;
+                keys[l] = a;
+              }
+            }
+          }
+          __syncthreads();
+        }
+      }
+      for (int e = threadIdx.x; e < n; e += kSegThreads) {
+        const int t = keys[e];
+        perm[q0 + e] = t;
+        col_idx[q0 + e] = cols[t];
+      }
+      __syncthreads();
     }
   }
 }
@@ -252,11 +408,60 @@ int grid_for(int64_t work, int threads) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(g, 148 * 32)));
 }
 
+// Tile sums and offsets of the multi-CTA scan (none when one CTA scans).
+size_t scan_tile_ints(int32_t n) {
+  return n > kScanSingleMax ? 2 * align_up(static_cast<size_t>((n + kScanTile - 1) / kScanTile + 1), 64) : 0;
+}
+
+// Counting workspace shared by the BSR build and the bucket sort: header
+// (error word, flags), per-bucket counts and fill counters, scan tiles.
+size_t count_ws_bytes(int32_t n) {
+  return kWorkspaceHeaderBytes + (2 * align_up(static_cast<size_t>(n), 64) + scan_tile_ints(n)) * sizeof(int);
+}
+
+int* scan_tiles_of(int* counts, int32_t n) { return counts + 2 * align_up(static_cast<size_t>(n), 64); }
+
+// Exclusive scan of n counts into out[0..n] (out[n] = total); flags[1]
+// receives the longest count.
+void launch_scan(const int* counts, int32_t n, int32_t* out, int* flags, int* tiles, cudaStream_t s) {
+  if (n <= kScanSingleMax) {
+    k_scan<<<1, kScanThreads, 0, s>>>(counts, n, out, flags);
+    return;
+  }
+  const int nt = (n + kScanTile - 1) / kScanTile;
+  int* tile_sum = tiles;
+  int* tile_off = tiles + align_up(static_cast<size_t>(nt + 1), 64);
+  k_tile_sums<<<nt, kScanThreads, 0, s>>>(counts, n, tile_sum, flags);
+  k_scan<<<1, kScanThreads, 0, s>>>(tile_sum, nt, tile_off, nullptr);
+  k_scan_apply<<<nt, kScanThreads, 0, s>>>(counts, n, tile_off, out);
+}
+
+kairo_status launch_segsort(const int32_t* cols, const int32_t* row_ptr, int32_t n, int32_t* col_idx, int32_t* perm,
+                            const int* flags, unsigned* err, bool long_ok, cudaStream_t s) {
+  static bool attr_set[64] = {false};
+  const int dev = current_device();
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&k_segsort),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kSortMax * static_cast<int>(sizeof(int)));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_segsort)");
+    attr_set[dev] = true;
+  }
+  // Two CTAs per SM; each takes `chunk` buckets (a multiple of 32) at a time.
+  constexpr int kCtas = 2 * 148;
+  int64_t chunk = (static_cast<int64_t>(n) + kCtas - 1) / kCtas;
+  chunk = std::min<int64_t>(kSegThreads, std::max<int64_t>(32, (chunk + 31) / 32 * 32));
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(kCtas, (n + chunk - 1) / chunk)));
+  k_segsort<<<grid, kSegThreads, kSortMax * sizeof(int), s>>>(cols, row_ptr, n, static_cast<int>(chunk), col_idx,
+                                                              perm, flags, err, long_ok);
+  return KAIRO_STATUS_SUCCESS;
+}
+
 }  // namespace
 
 size_t bsr_build_ws_bytes(int64_t num_tiles, int32_t nbr) {
   (void)num_tiles;
-  return kWorkspaceHeaderBytes + 2 * align_up(static_cast<size_t>(nbr), 64) * sizeof(int);
+  return count_ws_bytes(nbr);
 }
 
 }  // namespace kairo
@@ -286,20 +491,12 @@ extern "C" kairo_status kairo_bsr_build(const int32_t* tile_row_ids, const int32
   e = cudaMemsetAsync(workspace, 0, bsr_build_ws_bytes(num_tiles, nbr), s);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(build workspace)");
   if (num_tiles > 0) k_count<<<grid_for(num_tiles, 256), 256, 0, s>>>(tile_row_ids, tile_col_ids, num_tiles, nbr, nbc, w.counts, w.flags, w.err);
-  k_scan<<<1, kScanThreads, 0, s>>>(w.counts, nbr, row_ptr, w.flags);
+  launch_scan(w.counts, nbr, row_ptr, w.flags, scan_tiles_of(w.counts, nbr), s);
   if (num_tiles > 0) {
     k_place<<<grid_for(num_tiles, 256), 256, 0, s>>>(tile_row_ids, tile_col_ids, num_tiles, row_ptr, w.fill, col_idx,
                                                      perm, w.flags, w.err);
-    static bool attr_set[64] = {false};
-    const int dev = current_device();
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-      e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&k_segsort), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kSortMax * static_cast<int>(sizeof(int)));
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_segsort)");
-      attr_set[dev] = true;
-    }
-    k_segsort<<<std::max(1, std::min(nbr, 148 * 8)), 1024, kSortMax * sizeof(int), s>>>(tile_col_ids, row_ptr, nbr,
-                                                                                       col_idx, perm, w.flags, w.err);
+    kairo_status st = launch_segsort(tile_col_ids, row_ptr, nbr, col_idx, perm, w.flags, w.err, false, s);
+    if (st) return st;
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch of the BSR build kernels");
@@ -355,10 +552,8 @@ extern "C" kairo_status kairo_dense_to_tiles(const void* a, int64_t m, int64_t k
 namespace kairo {
 
 // Bucket-sort workspace: header (error word, flags), per-bucket counts and
-// fill counters.
-size_t bucket_sort_ws_bytes(int32_t nbuckets) {
-  return kWorkspaceHeaderBytes + 2 * align_up(static_cast<size_t>(nbuckets), 64) * sizeof(int);
-}
+// fill counters, scan tiles.
+size_t bucket_sort_ws_bytes(int32_t nbuckets) { return count_ws_bytes(nbuckets); }
 
 kairo_status bucket_sort(const int32_t* keys, const int32_t* vals, int32_t nvals, int64_t n, int32_t nbuckets,
                          int32_t* bucket_ptr, int32_t* perm, int32_t* vals_sorted, void* ws, cudaStream_t s,
@@ -374,19 +569,11 @@ kairo_status bucket_sort(const int32_t* keys, const int32_t* vals, int32_t nvals
   if (e == cudaSuccess) e = cudaMemsetAsync(flags, 1, 1, s);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(bucket-sort workspace)");
   if (n > 0) k_count<<<grid_for(n, 256), 256, 0, s>>>(keys, vals, n, nbuckets, nvals, counts, flags, err);
-  k_scan<<<1, kScanThreads, 0, s>>>(counts, nbuckets, bucket_ptr, flags);
+  launch_scan(counts, nbuckets, bucket_ptr, flags, scan_tiles_of(counts, nbuckets), s);
   if (n > 0) {
     k_place<<<grid_for(n, 256), 256, 0, s>>>(keys, vals, n, bucket_ptr, fill, vals_sorted, perm, flags, err);
-    static bool attr_set[64] = {false};
-    const int dev = current_device();
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-      e = cudaFuncSetAttribute(reinterpret_cast<const void*>(&k_segsort), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kSortMax * static_cast<int>(sizeof(int)));
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(k_segsort)");
-      attr_set[dev] = true;
-    }
-    k_segsort<<<std::max(1, std::min(nbuckets, 148 * 8)), 1024, kSortMax * sizeof(int), s>>>(
-        vals, bucket_ptr, nbuckets, vals_sorted, perm, flags, err, long_buckets_ok);
+    kairo_status st = launch_segsort(vals, bucket_ptr, nbuckets, vals_sorted, perm, flags, err, long_buckets_ok, s);
+    if (st) return st;
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch of the bucket-sort kernels");

@@ -81,6 +81,116 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) k_gather(const T* __restric
   }
 }
 
+// Row bitmask of a COO element mask: bit c % 32 of word c / 32 of row r is
+// set when (r, c) is an entry.  Entries outside [0, n_rows) x [0, n_cols)
+// are skipped.
+__global__ void k_mask_bits(const int64_t* __restrict__ rows, const int64_t* __restrict__ cols, int64_t nnz,
+                            int64_t n_rows, int64_t n_cols, int64_t words, uint32_t* __restrict__ bits) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nnz;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = rows[i], c = cols[i];
+    if (r < 0 || r >= n_rows || c < 0 || c >= n_cols) continue;
+    atomicOr(bits + r * words + (c >> 5), 1u << (c & 31));
+  }
+}
+
+// Masked gather from the row bitmask.  A warp takes IDS ids at a time (one
+// load by its first lanes) and then ROWS rows at once: each lane loads VEC
+// consecutive columns of every row (16-byte vectors when rows are 16-byte
+// aligned) and the mask word holding them, all in flight together, then
+// stores the masked rows.  Every access is coalesced.  Large batches take 32
+// ids per warp and 8 rows in flight; small ones 2 and 2, so that more warps
+// share the batch (a sweep over batch shapes on B200 put both within a few
+// percent of a device-to-device copy of the output's bytes).
+constexpr int kSmallBatch = 16384;
+
+template <int EB, int VEC>
+struct GatherVec;
+template <>
+struct GatherVec<4, 4> {  // 4 x fp32
+  using V = uint4;
+  __device__ static V apply(V v, uint32_t m) {
+    v.x = (m & 1u) ? v.x : 0u;
+    v.y = (m & 2u) ? v.y : 0u;
+    v.z = (m & 4u) ? v.z : 0u;
+    v.w = (m & 8u) ? v.w : 0u;
+    return v;
+  }
+};
+template <>
+struct GatherVec<2, 8> {  // 8 x 16-bit
+  using V = uint4;
+  __device__ static uint32_t pair(uint32_t w, uint32_t m2) {
+    return w & (((m2 & 1u) ? 0x0000ffffu : 0u) | ((m2 & 2u) ? 0xffff0000u : 0u));
+  }
+  __device__ static V apply(V v, uint32_t m) {
+    v.x = pair(v.x, m);
+    v.y = pair(v.y, m >> 2);
+    v.z = pair(v.z, m >> 4);
+    v.w = pair(v.w, m >> 6);
+    return v;
+  }
+};
+template <>
+struct GatherVec<4, 1> {
+  using V = uint32_t;
+  __device__ static V apply(V v, uint32_t m) { return (m & 1u) ? v : 0u; }
+};
+template <>
+struct GatherVec<2, 1> {
+  using V = uint16_t;
+  __device__ static V apply(V v, uint32_t m) { return (m & 1u) ? v : static_cast<uint16_t>(0); }
+};
+
+template <int EB, int VEC, int IDS, int ROWS>
+__global__ void __launch_bounds__(kWarpsPerCta * 32) k_gather_bits(const void* __restrict__ weight, int64_t n_rows,
+                                                                   int64_t dim, const uint32_t* __restrict__ bits,
+                                                                   int64_t words, const int64_t* __restrict__ ids,
+                                                                   int64_t nids, void* __restrict__ out) {
+  using G = GatherVec<EB, VEC>;
+  using V = typename G::V;
+  const V* w = static_cast<const V*>(weight);
+  V* o = static_cast<V*>(out);
+  const int64_t vdim = dim / VEC;  // vectors per row (dim is a multiple of VEC)
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * kWarpsPerCta;
+  for (int64_t b0 = (static_cast<int64_t>(blockIdx.x) * kWarpsPerCta + (threadIdx.x >> 5)) * IDS; b0 < nids;
+       b0 += warps * IDS) {
+    long long mine = -1;  // lane l < IDS: row of id b0 + l, or -1 (missing / out of range)
+    if (lane < IDS && b0 + lane < nids) {
+      const int64_t r = ids[b0 + lane];
+      mine = (r >= 0 && r < n_rows) ? r : -1;
+    }
+#pragma unroll 1
+    for (int u0 = 0; u0 < IDS; u0 += ROWS) {
+      const V* src[ROWS];         // weight row, or null for a zero row
+      const uint32_t* mrow[ROWS];  // its mask words
+#pragma unroll
+      for (int u = 0; u < ROWS; ++u) {
+        const long long r = __shfl_sync(0xffffffffu, mine, u0 + u);
+        src[u] = r >= 0 ? w + r * vdim : nullptr;
+        mrow[u] = bits + (r >= 0 ? r : 0) * words;
+      }
+      const int64_t nb = min(static_cast<int64_t>(ROWS), nids - (b0 + u0));  // rows to store
+      V* dst = o + (b0 + u0) * vdim;
+#pragma unroll 1
+      for (int64_t v = lane; v < vdim; v += 32) {
+        const int64_t c = v * VEC;  // first column of this lane's vector
+        V val[ROWS];
+        uint32_t m[ROWS];
+#pragma unroll
+        for (int u = 0; u < ROWS; ++u) {
+          val[u] = src[u] ? src[u][v] : V{};
+          m[u] = src[u] ? mrow[u][c >> 5] >> (c & 31) : 0u;
+        }
+#pragma unroll
+        for (int u = 0; u < ROWS; ++u)
+          if (u < nb) dst[u * vdim + v] = G::apply(val[u], m[u]);
+      }
+    }
+  }
+}
+
 // Bucket of every batch position: the index of batch_ids[b] in the sorted
 // active_ids, or nactive when it is not active.
 __global__ void k_scatter_keys(const int64_t* __restrict__ active_ids, int64_t nactive,
@@ -348,5 +458,62 @@ extern "C" kairo_status kairo_coo_sort_rows(const int64_t* rows, const int64_t* 
                                    cols_sorted, perm, static_cast<const unsigned*>(workspace));
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch of the mask widening kernel");
+  return KAIRO_STATUS_SUCCESS;
+}
+
+extern "C" kairo_status kairo_mask_bits(const int64_t* rows, const int64_t* cols, int64_t nnz, int64_t n_rows,
+                                        int64_t n_cols, uint32_t* bits, void* stream) {
+  if (n_rows < 0 || n_cols < 0 || nnz < 0) return fail(KAIRO_STATUS_INVALID_VALUE, "invalid size");
+  if (!bits && n_rows > 0 && n_cols > 0) return fail(KAIRO_STATUS_INVALID_VALUE, "null bits");
+  if (nnz > 0 && (!rows || !cols)) return fail(KAIRO_STATUS_INVALID_VALUE, "null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t words = (n_cols + 31) / 32;
+  if (n_rows > 0 && words > 0) {
+    cudaError_t e = cudaMemsetAsync(bits, 0, static_cast<size_t>(n_rows) * words * sizeof(uint32_t), s);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(mask bits)");
+  }
+  if (nnz > 0) {
+    const int g = std::max(1, static_cast<int>(std::min<int64_t>((nnz + 255) / 256, 148 * 16)));
+    k_mask_bits<<<g, 256, 0, s>>>(rows, cols, nnz, n_rows, n_cols, words, bits);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch of the mask bits kernel");
+  return KAIRO_STATUS_SUCCESS;
+}
+
+extern "C" kairo_status kairo_sparse_gather_bits(const void* weight, int64_t n_rows, int64_t dim, kairo_dtype dtype,
+                                                 const uint32_t* bits, const int64_t* ids, int64_t nids, void* out,
+                                                 void* stream) {
+  if (n_rows < 0 || dim <= 0 || nids < 0) return fail(KAIRO_STATUS_INVALID_VALUE, "invalid size");
+  if (dtype != KAIRO_DTYPE_F32 && dtype != KAIRO_DTYPE_F16 && dtype != KAIRO_DTYPE_BF16)
+    return fail(KAIRO_STATUS_INVALID_VALUE, "unknown dtype");
+  if (nids == 0) return KAIRO_STATUS_SUCCESS;
+  if (!weight || !bits || !ids || !out) return fail(KAIRO_STATUS_INVALID_VALUE, "null pointer argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int eb = static_cast<int>(dtype_bytes(dtype));
+  const int64_t words = (dim + 31) / 32;
+  const bool vec = (dim * eb) % 16 == 0 && reinterpret_cast<uintptr_t>(weight) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(out) % 16 == 0;
+  if (nids < kSmallBatch) {
+    const int g = warp_grid((nids + 1) / 2);
+    if (eb == 4) {
+      if (vec) k_gather_bits<4, 4, 2, 2><<<g, kWarpsPerCta * 32, 0, s>>>(weight, n_rows, dim, bits, words, ids, nids, out);
+      else k_gather_bits<4, 1, 2, 2><<<g, kWarpsPerCta * 32, 0, s>>>(weight, n_rows, dim, bits, words, ids, nids, out);
+    } else {
+      if (vec) k_gather_bits<2, 8, 2, 2><<<g, kWarpsPerCta * 32, 0, s>>>(weight, n_rows, dim, bits, words, ids, nids, out);
+      else k_gather_bits<2, 1, 2, 2><<<g, kWarpsPerCta * 32, 0, s>>>(weight, n_rows, dim, bits, words, ids, nids, out);
+    }
+  } else {
+    const int g = warp_grid((nids + 31) / 32);
+    if (eb == 4) {
+      if (vec) k_gather_bits<4, 4, 32, 8><<<g, kWarpsPerCta * 32, 0, s>>>(weight, n_rows, dim, bits, words, ids, nids, out);
+      else k_gather_bits<4, 1, 32, 8><<<g, kWarpsPerCta * 32, 0, s>>>(weight, n_rows, dim, bits, words, ids, nids, out);
+    } else {
+      if (vec) k_gather_bits<2, 8, 32, 8><<<g, kWarpsPerCta * 32, 0, s>>>(weight, n_rows, dim, bits, words, ids, nids, out);
+      else k_gather_bits<2, 1, 32, 8><<<g, kWarpsPerCta * 32, 0, s>>>(weight, n_rows, dim, bits, words, ids, nids, out);
+    }
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch of the sparse gather kernel");
   return KAIRO_STATUS_SUCCESS;
 }

@@ -39,12 +39,15 @@ class MaskRows:
     """A COO element mask in row order (the reference's CSR view of it).
 
     row_offsets: (N + 1,) int64; rows/cols: (nnz,) int64 sorted stably by
-    row; perm: (nnz,) int64, the mask position of every sorted entry."""
+    row; perm: (nnz,) int64, the mask position of every sorted entry;
+    bits: (N, ceil(D / 32)) int32 words, bit c % 32 of word c / 32 set for
+    an active (row, c) -- what the gather kernel reads."""
 
     row_offsets: Tensor
     rows: Tensor
     cols: Tensor
     perm: Tensor
+    bits: Tensor
     dense_shape: tuple[int, int]
 
     @property
@@ -87,7 +90,12 @@ def sort_mask_rows(mask: SparseMask, device: torch.device | str | None = None, *
                                            _lib.stream_handle(dev)), "sort_mask_rows")
         if check:
             _lib.raise_on_device_error(ws)
-    return MaskRows(row_offsets=row_offsets, rows=rows_s, cols=cols_s, perm=perm, dense_shape=(n_rows, n_cols))
+        bits = torch.empty(n_rows, (n_cols + 31) // 32, dtype=torch.int32, device=dev)
+        _lib.check(lib.kairo_mask_bits(_lib.ptr(rows) if nnz else None, _lib.ptr(cols) if nnz else None, nnz, n_rows,
+                                       n_cols, bits.data_ptr() if bits.numel() else None, _lib.stream_handle(dev)),
+                   "sort_mask_rows")
+    return MaskRows(row_offsets=row_offsets, rows=rows_s, cols=cols_s, perm=perm, bits=bits,
+                    dense_shape=(n_rows, n_cols))
 
 
 # Row-sorted view of every SparseMask object used with sparse_gather, per
@@ -117,10 +125,9 @@ def _gather(weight: Tensor, mr: MaskRows, ids: Tensor) -> Tensor:
     if ids.numel() == 0:
         return out
     with torch.cuda.device(weight.device):
-        _lib.check(_lib.lib().kairo_sparse_gather(weight.data_ptr(), n, d, _lib.kairo_dtype(weight.dtype),
-                                                  mr.row_offsets.data_ptr(),
-                                                  _lib.ptr(mr.cols) if mr.nnz else None, mr.nnz, ids.data_ptr(),
-                                                  ids.numel(), out.data_ptr(), _lib.stream_handle(weight.device)),
+        _lib.check(_lib.lib().kairo_sparse_gather_bits(weight.data_ptr(), n, d, _lib.kairo_dtype(weight.dtype),
+                                                       mr.bits.data_ptr(), ids.data_ptr(), ids.numel(),
+                                                       out.data_ptr(), _lib.stream_handle(weight.device)),
                    "sparse_gather")
     return out
 
@@ -136,8 +143,8 @@ def sparse_gather(weight: Tensor, mask: SparseMask | MaskRows, ids: Tensor) -> T
     if ids.numel() == 0:
         return torch.zeros(0, weight.shape[1], dtype=weight.dtype, device=weight.device)
     mr = mask if isinstance(mask, MaskRows) else _mask_rows_cached(mask, weight.device)
-    if mr.row_offsets.numel() < weight.shape[0] + 1:
-        raise ValueError(f"the mask covers {mr.row_offsets.numel() - 1} rows; weight has {weight.shape[0]}")
+    if tuple(mr.dense_shape) != tuple(weight.shape):
+        raise ValueError(f"the mask is {tuple(mr.dense_shape)}; weight is {tuple(weight.shape)}")
     ids = ids.to(device=weight.device, dtype=torch.int64).reshape(-1).contiguous()
     return _gather(weight.contiguous(), mr, ids)
 

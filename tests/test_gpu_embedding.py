@@ -89,7 +89,8 @@ def _random_mask(n, d, density, seed, shuffle=True):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("shape", [(1000, 64, 0.2, 4096), (5000, 300, 0.05, 1000), (64, 5000, 0.6, 129)])
+@pytest.mark.parametrize("shape", [(1000, 64, 0.2, 4096), (5000, 300, 0.05, 1000), (64, 5000, 0.6, 129),
+                                   (3000, 96, 0.3, 20001)])   # a large batch: 32 ids per warp
 def test_gather_vs_oracle(dtype, shape):
     n, d, density, b = shape
     m = _random_mask(n, d, density, seed=n + d)
@@ -104,6 +105,14 @@ def test_gather_vs_oracle(dtype, shape):
     exp = oracle.sparse_gather(w, oracle.row_offsets(rs, n), cs, ids)
     assert got.dtype == dtype
     assert torch.equal(_bits(got), _bits(exp))
+    # the row-offset kernel behind the reference's extension entry point
+    got_csr = _C.sparse_gather_forward(w.to(DEV), mr.rows, mr.cols, ids.to(DEV), mr.row_offsets)
+    assert torch.equal(_bits(got_csr), _bits(exp))
+    # a weight that is not 16-byte aligned takes the scalar path
+    flat = torch.empty(n * d + 1, dtype=dtype, device=DEV)
+    wm = flat[1:].view(n, d)
+    wm.copy_(w.to(DEV))
+    assert torch.equal(_bits(sparse_gather(wm, mr, ids.to(DEV))), _bits(exp))
 
 
 def test_gather_long_rows_and_cache():

@@ -72,6 +72,26 @@ def test_bsr_build_zipf_long_rows_unsorted():
     assert torch.equal(a.blk_idx.cpu().to(torch.int64), perm)
 
 
+@pytest.mark.parametrize("nbr,nbc,per_row", [(50000, 64, 3), (40, 8192, 2000), (20000, 256, 40)])
+def test_bsr_build_unsorted_many_and_long_rows(nbr, nbc, per_row):
+    """Unsorted tile lists: more block-rows than one CTA scans (the
+    multi-CTA scan), rows of up to 32 tiles (sorted in registers by a warp)
+    and longer rows (sorted in shared memory)."""
+    g = torch.Generator().manual_seed(nbr)
+    lens = torch.randint(0, 2 * per_row + 1, (nbr,), generator=g).clamp(max=nbc)
+    rows = torch.repeat_interleave(torch.arange(nbr), lens)
+    cols = torch.cat([torch.randperm(nbc, generator=g)[:int(n)] for n in lens])
+    sh = torch.randperm(rows.numel(), generator=g)
+    rows, cols = rows[sh].contiguous(), cols[sh].contiguous()
+    tiles = torch.zeros(rows.numel(), 16, 16, dtype=torch.float16, device=DEV)
+    a = bsr_from_tiles(tiles, rows.to(DEV), cols.to(DEV), (nbr * 16, nbc * 16))
+    perm, rows_s, cols_s = oracle.sort_coo_by_row(rows, cols, nbr)
+    assert torch.equal(a.row_ptr.cpu().to(torch.int64), oracle.row_offsets(rows_s, nbr))
+    assert torch.equal(a.col_idx.cpu().to(torch.int64), cols_s)
+    assert torch.equal(a.blk_idx.cpu().to(torch.int64), perm)
+    assert a.max_row_blocks == int(lens.max())
+
+
 def test_bsr_build_rejects_bad_ids():
     tiles = torch.zeros(2, 16, 16, device=DEV, dtype=torch.float16)
     rows = torch.tensor([0, 5], device=DEV, dtype=torch.int32)
