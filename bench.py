@@ -459,6 +459,93 @@ def run_e2e(args, spec, a, b, out, cfg, dev, stream, linear, world, dist):
             "path": "pinned host -> device copies, kairo_b200.ops.block_sparse_mm_bsr, device -> pinned host"}
 
 
+# ---------------------------------------------------------------- backward
+
+def run_backward(args) -> None:
+    """One training-step backward of the linear layer Y = X @ W^T with the
+    linear-layer workload's weight: refresh W^T's values, dX = dY @ W (the
+    LINEAR SpMM on W^T) and dW on W's nonzero blocks (SDDMM, bf16 output).
+    Each part is timed with its own CUDA events; the step is their sum."""
+    from kairo_b200.ops import (bsr_from_tiles, bsr_transpose, describe, sparse_linear, sparse_linear_weight_grad,
+                                transpose_values)
+
+    rank, world, local = dist_env()
+    if world > 1:
+        raise SystemExit("--op backward runs on one GPU")
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    spec = WORKLOADS[args.workload if args.workload != "bf16_uniform" else "bf16_linear"]
+    if args.shape:
+        m, k, n = (int(x) for x in args.shape.lower().split("x"))
+        spec = spec.scaled(m, k, n)
+    if spec.layout != "linear":
+        raise SystemExit("--op backward needs a linear-layout workload (bf16_linear)")
+    problem = generate(spec, seed=args.seed, device=dev)
+    w = bsr_from_tiles(problem.tiles, problem.row_ids, problem.col_ids, (spec.m, spec.k))
+    x = problem.b                                     # (batch, in_features)
+    g = torch.Generator(device=dev).manual_seed(args.seed + 1)
+    dy = torch.randn(spec.n, spec.m, generator=g, device=dev).to(spec.dtype)
+    wt = bsr_transpose(w, check=True)
+    dx = torch.empty(spec.n, spec.k, dtype=spec.dtype, device=dev)
+    parts = ("wt_values", "dx", "dw")
+
+    def part(name):
+        if name == "wt_values":
+            transpose_values(w, wt)
+        elif name == "dx":
+            sparse_linear(dy, wt.matrix, out=dx)
+        else:
+            sparse_linear_weight_grad(dy, x, w, wt, out_dtype=spec.dtype)
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    times = {p: [] for p in parts}
+    sampler = ClockSampler(dev)
+    with sampler:
+        for i in range(args.warmup + args.steps):
+            for p in parts:
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                part(p)
+                e1.record(stream)
+                if i >= args.warmup:
+                    times[p].append((e0, e1))
+        torch.cuda.synchronize()
+    ms = {p: sum(a.elapsed_time(b) for a, b in times[p]) / args.steps for p in parts}
+    step_ms = sum(ms.values())
+    fl = flops(spec)  # one product: 2 * nnzb * bm * bk * batch
+    peaks, peak_kind = measured_peaks()
+    tpeak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    sdd_tflops = fl / (ms["dw"] / 1e3) / 1e12
+    line = {
+        "metric": "linear_backward_tflops",
+        "value": 2 * fl / (step_ms / 1e3) / 1e12,
+        "unit": "TFLOP/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": step_ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": str(spec.dtype).replace("torch.", ""),
+        "data": "synthetic (seeded, generated on device)",
+        "config": {"workload": spec.name, "m": spec.m, "k": spec.k, "batch": spec.n, "block": spec.block,
+                   "sparsity": spec.sparsity, "nnzb": w.nnzb, "parts_ms": ms,
+                   "l2": "flushed before every part (256 MiB write, untimed)"},
+        "roofline": {"bound": "tensor", "kernel": "bsr_sddmm_tc (dW)", "achieved": sdd_tflops, "peak": tpeak,
+                     "unit": "TFLOP/s", "frac": sdd_tflops / tpeak, "traffic": None, "peak_kind": peak_kind},
+        "cpu_baseline": None,
+        # values refresh 1, dX per its plan, dW: stack list + SDDMM 2
+        "gpu_launches": args.steps * (1 + describe(wt.matrix, spec.n, linear=True)["launches"] + 2),
+        "clocks": sampler.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ---------------------------------------------------------------- embedding ops
 
 EMB_WORKLOADS = {
@@ -674,8 +761,9 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=3.0)
-    ap.add_argument("--op", choices=("spmm", "gather", "scatter"), default="spmm",
-                    help="spmm (default): the block-sparse SpMM; gather/scatter: the masked embedding ops")
+    ap.add_argument("--op", choices=("spmm", "backward", "gather", "scatter"), default="spmm",
+                    help="spmm (default): the block-sparse SpMM; backward: the linear layer's dX and dW; "
+                         "gather/scatter: the masked embedding ops")
     ap.add_argument("--emb-workload", choices=sorted(EMB_WORKLOADS), default="emb_large")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -683,7 +771,10 @@ def main() -> None:
     if args.op != "spmm":
         if args.impl == "reference":
             raise SystemExit("--impl reference times the SpMM path only")
-        run_embedding(args)
+        if args.op == "backward":
+            run_backward(args)
+        else:
+            run_embedding(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
