@@ -405,7 +405,11 @@ def run_ours(args) -> None:
 def run_e2e(args, spec, a, b, out, cfg, dev, stream, linear, world, dist):
     """Same metric through the public operator with host (pinned) buffers:
     every step copies this rank's blocks, indices and B to the device and
-    reads C back; the copies are inside the timed region."""
+    reads C back; the copies are inside the timed region.  Consecutive steps
+    are pipelined the way a serving loop overlaps requests: two device buffer
+    sets and three streams (upload, compute, read-back), so step i's read-back
+    runs while step i+1 uploads (PCIe is full duplex).  A set is reused only
+    after its previous read-back has finished."""
     from kairo_b200.ops import block_sparse_mm_bsr, sparse_linear
     from kairo_b200.types import BlockSparseMatrix
 
@@ -413,35 +417,57 @@ def run_e2e(args, spec, a, b, out, cfg, dev, stream, linear, world, dist):
     h_rp = a.row_ptr.to("cpu").pin_memory()
     h_ci = a.col_idx.to("cpu").pin_memory()
     h_b = b.to("cpu").pin_memory()
-    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    d_blocks = torch.empty_like(a.blocks)
-    d_rp = torch.empty_like(a.row_ptr)
-    d_ci = torch.empty_like(a.col_idx)
-    d_b = torch.empty_like(b)
+    h_out = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
+    sets = [{"blocks": torch.empty_like(a.blocks), "rp": torch.empty_like(a.row_ptr),
+             "ci": torch.empty_like(a.col_idx), "b": torch.empty_like(b),
+             "out": out if j == 0 else torch.empty_like(out)} for j in range(2)]
+    s_in = torch.cuda.Stream(dev)
+    s_out = torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_c = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
+    used = [False, False]
     steps = max(1, min(args.steps, args.e2e_steps))
 
-    def one():
-        d_blocks.copy_(h_blocks, non_blocking=True)
-        d_rp.copy_(h_rp, non_blocking=True)
-        d_ci.copy_(h_ci, non_blocking=True)
-        d_b.copy_(h_b, non_blocking=True)
-        m = BlockSparseMatrix(row_ptr=d_rp, col_idx=d_ci, blocks=d_blocks, shape=a.shape, block_size=a.block_size,
-                              max_row_blocks=a.max_row_blocks)
+    def one(i):
+        j = i % 2
+        d = sets[j]
+        with torch.cuda.stream(s_in):
+            if used[j]:
+                s_in.wait_event(ev_out[j])   # set j's last read-back (and so its compute) is done
+            d["blocks"].copy_(h_blocks, non_blocking=True)
+            d["rp"].copy_(h_rp, non_blocking=True)
+            d["ci"].copy_(h_ci, non_blocking=True)
+            d["b"].copy_(h_b, non_blocking=True)
+            ev_in[j].record(s_in)
+        used[j] = True
+        stream.wait_event(ev_in[j])
+        m = BlockSparseMatrix(row_ptr=d["rp"], col_idx=d["ci"], blocks=d["blocks"], shape=a.shape,
+                              block_size=a.block_size, max_row_blocks=a.max_row_blocks)
         if linear:
-            sparse_linear(d_b, m, out=out, config=cfg)
+            sparse_linear(d["b"], m, out=d["out"], config=cfg)
         else:
-            block_sparse_mm_bsr(m, d_b, out=out, config=cfg)
-        h_out.copy_(out, non_blocking=True)
+            block_sparse_mm_bsr(m, d["b"], out=d["out"], config=cfg)
+        ev_c[j].record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(ev_c[j])
+            h_out[j].copy_(d["out"], non_blocking=True)
+            ev_out[j].record(s_out)
+        return j
 
-    one()
+    for i in range(2):  # warm-up of both sets
+        one(i)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(steps):
-        one()
+    e0.record(s_in)
+    last = 0
+    for i in range(steps):
+        last = one(i)
+    stream.wait_event(ev_out[last])
+    stream.wait_event(ev_out[1 - last])
     e1.record(stream)
     torch.cuda.synchronize()
     t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
@@ -449,14 +475,15 @@ def run_e2e(args, spec, a, b, out, cfg, dev, stream, linear, world, dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = t.item()
     h2d = h_blocks.numel() * h_blocks.element_size() + h_rp.numel() * 4 + h_ci.numel() * 4 + h_b.numel() * h_b.element_size()
-    d2h = h_out.numel() * h_out.element_size()
+    d2h = h_out[0].numel() * h_out[0].element_size()
     if world > 1:
         tb = torch.tensor([float(h2d), float(d2h)], dtype=torch.float64, device=dev)
         dist.all_reduce(tb, op=dist.ReduceOp.SUM)
         h2d, d2h = int(tb[0].item()), int(tb[1].item())
     return {"value": flops(spec) / (ms / 1e3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": steps,
-            "path": "pinned host -> device copies, kairo_b200.ops.block_sparse_mm_bsr, device -> pinned host"}
+            "path": "pinned host -> device copies, kairo_b200.ops.block_sparse_mm_bsr, device -> pinned host; "
+                    "consecutive steps overlapped on upload / compute / read-back streams"}
 
 
 # ---------------------------------------------------------------- backward
@@ -757,7 +784,7 @@ def main() -> None:
     ap.add_argument("--band-rows", type=int, default=0)
     ap.add_argument("--gather", action="store_true", help="also time the all-gather of C (reported separately)")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=3.0)

@@ -369,6 +369,50 @@ __global__ void __launch_bounds__(256) k_transpose_blocks(const T* __restrict__ 
   }
 }
 
+// The same with 16-byte vectors (VE elements) on both sides: rows of bk and
+// bm elements are multiples of VE, blocks 16-byte aligned.  A block is read
+// as row vectors into a padded shared tile, and written as row vectors of
+// the transposed block gathered down the tile's columns (the padding puts
+// the rows of one column in different banks).
+template <typename T>
+__global__ void __launch_bounds__(256) k_transpose_blocks_vec(const T* __restrict__ blocks,
+                                                              const int32_t* __restrict__ blk_idx,
+                                                              const int32_t* __restrict__ perm_t, int64_t nnzb,
+                                                              int64_t nstored, int32_t bm, int32_t bk,
+                                                              T* __restrict__ out, unsigned* err) {
+  constexpr int VE = 16 / sizeof(T);
+  constexpr int kPitch = 64 + 4 / sizeof(T);  // elements per tile row: an odd number of 4-byte words
+  __shared__ __align__(16) T tile[64 * kPitch];
+  const int row_vecs = bk / VE;       // input vectors per block row
+  const int out_vecs = bm / VE;       // output vectors per transposed row
+  const int nvec = bm * row_vecs;     // vectors per block
+  for (int64_t q = blockIdx.x; q < nnzb; q += gridDim.x) {
+    const int64_t p = perm_t[q];
+    const int64_t sidx = (p >= 0 && p < nnzb) ? (blk_idx ? static_cast<int64_t>(blk_idx[p]) : p) : -1;
+    const bool ok = sidx >= 0 && sidx < nstored;
+    if (!ok && threadIdx.x == 0) atomicCAS(err, 0u, KAIRO_DEVERR_BAD_INDEX);
+    const uint4* src = reinterpret_cast<const uint4*>(blocks + (ok ? sidx : 0) * bm * bk);
+    for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+      const int r = v / row_vecs, c0 = (v - r * row_vecs) * VE;
+      const uint4 x = ok ? src[v] : make_uint4(0u, 0u, 0u, 0u);
+      const T* xe = reinterpret_cast<const T*>(&x);
+#pragma unroll
+      for (int i = 0; i < VE; ++i) tile[r * kPitch + c0 + i] = xe[i];
+    }
+    __syncthreads();
+    uint4* dst = reinterpret_cast<uint4*>(out + q * bm * bk);  // (bk x bm) row-major
+    for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+      const int c = v / out_vecs, r0 = (v - c * out_vecs) * VE;
+      uint4 y;
+      T* ye = reinterpret_cast<T*>(&y);
+#pragma unroll
+      for (int i = 0; i < VE; ++i) ye[i] = tile[(r0 + i) * kPitch + c];
+      dst[v] = y;
+    }
+    __syncthreads();
+  }
+}
+
 // Dense (M x K) -> tiles (num_tiles, tile, tile), zero-padded at the edges.
 // One thread copies one tile row segment of up to 8 elements.
 template <typename T>
@@ -598,6 +642,33 @@ kairo_status transpose_values(const kairo_bsr* a, const int32_t* perm_t, void* b
   if (a->nnzb == 0) return KAIRO_STATUS_SUCCESS;
   if (a->bm > 64 || a->bk > 64) return fail(KAIRO_STATUS_NOT_SUPPORTED, "transpose supports blocks up to 64 x 64");
   const int g = static_cast<int>(std::min<int64_t>(a->nnzb, 148 * 16));
+  const int ve = a->dtype == KAIRO_DTYPE_F32 ? 4 : 8;
+  const bool vec = a->bm % ve == 0 && a->bk % ve == 0 && reinterpret_cast<uintptr_t>(a->blocks) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(blocks_t) % 16 == 0;
+  if (vec) {
+    switch (a->dtype) {
+      case KAIRO_DTYPE_F32:
+        k_transpose_blocks_vec<float><<<g, 256, 0, s>>>(static_cast<const float*>(a->blocks), a->blk_idx, perm_t,
+                                                        a->nnzb, a->nblocks_stored, a->bm, a->bk,
+                                                        static_cast<float*>(blocks_t), err);
+        break;
+      case KAIRO_DTYPE_F16:
+        k_transpose_blocks_vec<__half><<<g, 256, 0, s>>>(static_cast<const __half*>(a->blocks), a->blk_idx, perm_t,
+                                                         a->nnzb, a->nblocks_stored, a->bm, a->bk,
+                                                         static_cast<__half*>(blocks_t), err);
+        break;
+      case KAIRO_DTYPE_BF16:
+        k_transpose_blocks_vec<__nv_bfloat16><<<g, 256, 0, s>>>(
+            static_cast<const __nv_bfloat16*>(a->blocks), a->blk_idx, perm_t, a->nnzb, a->nblocks_stored, a->bm,
+            a->bk, static_cast<__nv_bfloat16*>(blocks_t), err);
+        break;
+      default:
+        return fail(KAIRO_STATUS_INVALID_VALUE, "unknown dtype");
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "launch of the block transpose kernel");
+    return KAIRO_STATUS_SUCCESS;
+  }
   switch (a->dtype) {
     case KAIRO_DTYPE_F32:
       k_transpose_blocks<float><<<g, 256, 0, s>>>(static_cast<const float*>(a->blocks), a->blk_idx, perm_t, a->nnzb,

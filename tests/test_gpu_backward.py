@@ -63,6 +63,20 @@ def test_transpose_bit_exact(case):
     assert t.matrix.shape == (k, m) and t.matrix.block_size == (bs, bs)
 
 
+def test_transpose_unaligned_blocks():
+    """Blocks not 16-byte aligned take the element-wise transpose kernel."""
+    w, _ = _weight(torch.bfloat16, 256, 512, 32, 0.7, seed=13)
+    stored = w.blocks if w.blk_idx is None else w.blocks[w.blk_idx.long()]
+    flat = torch.empty(stored.numel() + 1, dtype=stored.dtype, device=DEV)
+    shifted = flat[1:].view(stored.shape)
+    shifted.copy_(stored)
+    ws = BlockSparseMatrix(row_ptr=w.row_ptr, col_idx=w.col_idx, blocks=shifted, shape=w.shape,
+                           block_size=w.block_size)
+    t = bsr_transpose(ws, check=True)
+    _, _, pt = oracle.bsr_transpose(w.row_ptr, w.col_idx, w.nbc)
+    assert torch.equal(t.matrix.blocks, stored[pt.to(DEV).long()].transpose(1, 2))
+
+
 def test_transpose_empty_and_bad_index():
     w, _ = _weight(torch.float16, 128, 128, 32, 0.5, seed=4)
     e = BlockSparseMatrix(row_ptr=torch.zeros(w.nbr + 1, dtype=torch.int32, device=DEV),
