@@ -9,6 +9,7 @@
 // there are no atomics and every C element (including all-zero block-rows) is
 // written exactly once.
 #include <cuda_bf16.h>
+#include <algorithm>
 #include <cuda_fp16.h>
 
 #include "internal.h"
@@ -88,6 +89,122 @@ __global__ void __launch_bounds__(kSimtCols)
   }
 }
 
+// Row-staged variant for bk in {16, 32, 64}.  A CTA owns one block-row x 128
+// columns with KS thread groups of 128: the row's blocks are staged in
+// shared memory a chunk at a time (one pair of barriers per chunk, not per
+// block), group g takes blocks g, g + KS, ... of the chunk, and each thread
+// issues the BK loads of its B column for a block together (the k loop is
+// unrolled) before the FMAs.  The groups' partial sums are added in group
+// order at the end, so the result is deterministic.
+template <int BM_CAP, int BK, int KS, typename TIn>
+__global__ void __launch_bounds__(kSimtCols * KS)
+    bsr_spmm_simt_rows_kernel(const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx,
+                              const int32_t* __restrict__ blk_idx, const TIn* __restrict__ blocks,
+                              const TIn* __restrict__ b, int64_t ldb, float* __restrict__ c, int64_t ldc, int32_t m,
+                              int64_t k, int32_t n, int32_t bm, int32_t nbc, int64_t nblocks_stored, int chunk_cap,
+                              unsigned* err) {
+  constexpr int BLK_F = BK * BM_CAP;  // floats of one staged block: As[kk][r]
+  extern __shared__ __align__(16) float sm[];
+  const int i = blockIdx.x;
+  const int tcol = threadIdx.x % kSimtCols;
+  const int g = threadIdx.x / kSimtCols;
+  const int col = blockIdx.y * kSimtCols + tcol;
+  float acc[BM_CAP];
+#pragma unroll
+  for (int r = 0; r < BM_CAP; ++r) acc[r] = 0.f;
+  const int p_begin = row_ptr[i];
+  const int p_end = row_ptr[i + 1];
+  const int blk_elems = bm * BK;
+  for (int c0 = p_begin; c0 < p_end; c0 += chunk_cap) {
+    const int cn = min(chunk_cap, p_end - c0);
+    __syncthreads();  // the previous chunk has been consumed
+    for (int e = threadIdx.x; e < cn * blk_elems; e += blockDim.x) {
+      const int j = e / blk_elems;
+      const int rem = e - j * blk_elems;
+      const int r = rem / BK, kk = rem - r * BK;
+      const int64_t blk = blk_idx ? static_cast<int64_t>(blk_idx[c0 + j]) : static_cast<int64_t>(c0 + j);
+      float v = 0.f;
+      if (blk >= 0 && blk < nblocks_stored) v = to_f32(blocks[blk * blk_elems + rem]);
+      else if (rem == 0) atomicCAS(err, 0u, KAIRO_DEVERR_BAD_INDEX);
+      sm[j * BLK_F + kk * BM_CAP + r] = v;
+    }
+    __syncthreads();
+    if (col < n) {
+      for (int j = g; j < cn; j += KS) {
+        const int cb = col_idx[c0 + j];
+        if (cb < 0 || cb >= nbc) {
+          if (tcol == 0) atomicCAS(err, 0u, KAIRO_DEVERR_BAD_INDEX);
+          continue;
+        }
+        const int64_t k0 = static_cast<int64_t>(cb) * BK;
+        float bv[BK];
+#pragma unroll
+        for (int kk = 0; kk < BK; ++kk) bv[kk] = (k0 + kk < k) ? to_f32(b[(k0 + kk) * ldb + col]) : 0.f;
+        const float4* a4 = reinterpret_cast<const float4*>(sm + j * BLK_F);
+#pragma unroll
+        for (int kk = 0; kk < BK; ++kk) {
+#pragma unroll
+          for (int r4 = 0; r4 < BM_CAP / 4; ++r4) {
+            const float4 a = a4[kk * (BM_CAP / 4) + r4];
+            acc[4 * r4 + 0] = fmaf(a.x, bv[kk], acc[4 * r4 + 0]);
+            acc[4 * r4 + 1] = fmaf(a.y, bv[kk], acc[4 * r4 + 1]);
+            acc[4 * r4 + 2] = fmaf(a.z, bv[kk], acc[4 * r4 + 2]);
+            acc[4 * r4 + 3] = fmaf(a.w, bv[kk], acc[4 * r4 + 3]);
+          }
+        }
+      }
+    }
+  }
+  if constexpr (KS > 1) {
+    // Partial sums of groups 1..KS-1 through shared memory, added in order.
+    __syncthreads();
+    float* red = sm;  // [KS-1][BM_CAP][128]
+    if (g > 0) {
+#pragma unroll
+      for (int r = 0; r < BM_CAP; ++r) red[((g - 1) * BM_CAP + r) * kSimtCols + tcol] = acc[r];
+    }
+    __syncthreads();
+    if (g > 0) return;
+#pragma unroll
+    for (int gg = 1; gg < KS; ++gg)
+#pragma unroll
+      for (int r = 0; r < BM_CAP; ++r) acc[r] += red[((gg - 1) * BM_CAP + r) * kSimtCols + tcol];
+  }
+  if (col < n) {
+#pragma unroll
+    for (int r = 0; r < BM_CAP; ++r) {
+      const int64_t row = static_cast<int64_t>(i) * bm + r;
+      if (r < bm && row < m) c[row * ldc + col] = acc[r];
+    }
+  }
+}
+
+// Shared-memory budget of the row-staged kernel's block chunk.
+constexpr int kChunkBytes = 32 * 1024;
+
+template <int BM_CAP, int BK, int KS, typename TIn>
+kairo_status launch_rows(const kairo_bsr* a, const void* b, int64_t ldb, int64_t n, void* c, int64_t ldc,
+                         void* workspace, cudaStream_t stream) {
+  constexpr int blk_bytes = BK * BM_CAP * 4;
+  const int chunk = std::max(KS, kChunkBytes / blk_bytes);
+  const size_t smem = std::max<size_t>(static_cast<size_t>(chunk) * blk_bytes,
+                                       static_cast<size_t>(KS - 1) * BM_CAP * kSimtCols * 4);
+  auto fn = &bsr_spmm_simt_rows_kernel<BM_CAP, BK, KS, TIn>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(SIMT SpMM)");
+  }
+  dim3 grid(static_cast<unsigned>(a->nbr), static_cast<unsigned>(ceil_div64(n, kSimtCols)));
+  fn<<<grid, kSimtCols * KS, smem, stream>>>(
+      a->row_ptr, a->col_idx, a->blk_idx, static_cast<const TIn*>(a->blocks), static_cast<const TIn*>(b), ldb,
+      static_cast<float*>(c), ldc, static_cast<int32_t>(a->rows), a->cols, static_cast<int32_t>(n), a->bm,
+      static_cast<int32_t>(ceil_div64(a->cols, a->bk)), a->nblocks_stored, chunk, static_cast<unsigned*>(workspace));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch of the SIMT SpMM kernel");
+  return KAIRO_STATUS_SUCCESS;
+}
+
 template <int BM_CAP, typename TIn>
 kairo_status launch_cap(const kairo_bsr* a, const void* b, int64_t ldb, int64_t n, void* c, int64_t ldc,
                         void* workspace, cudaStream_t stream) {
@@ -106,6 +223,9 @@ kairo_status launch_cap(const kairo_bsr* a, const void* b, int64_t ldb, int64_t 
 template <typename TIn>
 kairo_status launch_typed(const kairo_bsr* a, const void* b, int64_t ldb, int64_t n, void* c, int64_t ldc,
                           void* workspace, cudaStream_t stream) {
+  if (a->bk == 16 && a->bm <= 16) return launch_rows<16, 16, 4, TIn>(a, b, ldb, n, c, ldc, workspace, stream);
+  if (a->bk == 32 && a->bm <= 32) return launch_rows<32, 32, 2, TIn>(a, b, ldb, n, c, ldc, workspace, stream);
+  if (a->bk == 64 && a->bm <= 64) return launch_rows<64, 64, 1, TIn>(a, b, ldb, n, c, ldc, workspace, stream);
   if (a->bm <= 16) return launch_cap<16, TIn>(a, b, ldb, n, c, ldc, workspace, stream);
   if (a->bm <= 32) return launch_cap<32, TIn>(a, b, ldb, n, c, ldc, workspace, stream);
   return launch_cap<64, TIn>(a, b, ldb, n, c, ldc, workspace, stream);

@@ -167,6 +167,28 @@ def test_simt_spmm_vs_oracle(dtype, shape):
     assert err <= TOL, f"relative Frobenius error {err:.3e}"
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("bm,bk", [(16, 8), (8, 16), (24, 32), (64, 16)])
+def test_simt_spmm_rectangular_blocks(dtype, bm, bk):
+    """Non-square blocks (bk outside 16/32/64 takes the per-block kernel, the
+    others the row-staged one with bm below its register bound), against a
+    dense float64 product of the same BSR matrix."""
+    g = torch.Generator().manual_seed(bm * 100 + bk)
+    nbr, nbc, n = 40, 30, 100
+    keep = torch.rand(nbr, nbc, generator=g) < 0.3
+    rows, cols = keep.nonzero(as_tuple=True)
+    tiles = torch.randn(rows.numel(), bm, bk, generator=g).to(dtype)
+    b = torch.randn(nbc * bk, n, generator=g).to(dtype)
+    a = bsr_from_tiles(tiles.to(DEV), rows.to(DEV), cols.to(DEV), (nbr * bm, nbc * bk))
+    c = block_sparse_mm_bsr(a, b.to(DEV), config=KernelConfig(kernel="simt"), check=True)
+    dense = torch.zeros(nbr * bm, nbc * bk, dtype=torch.float64)
+    for t in range(rows.numel()):
+        r, q = int(rows[t]), int(cols[t])
+        dense[r * bm:(r + 1) * bm, q * bk:(q + 1) * bk] = tiles[t].double()
+    ref = dense @ b.double()
+    assert rel_fro(c, ref) <= TOL
+
+
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("shape", [(256, 512, 256, 64, 0.8, 256), (512, 1024, 300, 32, 0.9, 128),
                                    (128, 256, 128, 16, 0.5, 0)])
