@@ -493,8 +493,8 @@ def run_backward(args) -> None:
     linear-layer workload's weight: refresh W^T's values, dX = dY @ W (the
     LINEAR SpMM on W^T) and dW on W's nonzero blocks (SDDMM, bf16 output).
     Each part is timed with its own CUDA events; the step is their sum."""
-    from kairo_b200.ops import (bsr_from_tiles, bsr_transpose, describe, sparse_linear, sparse_linear_weight_grad,
-                                transpose_values)
+    from kairo_b200.ops import (KernelConfig, bsr_from_tiles, bsr_transpose, describe, sparse_linear,
+                                sparse_linear_weight_grad, transpose_values)
 
     rank, world, local = dist_env()
     if world > 1:
@@ -516,13 +516,15 @@ def run_backward(args) -> None:
     dy = torch.randn(spec.n, spec.m, generator=g, device=dev).to(spec.dtype)
     wt = bsr_transpose(w, check=True)
     dx = torch.empty(spec.n, spec.k, dtype=spec.dtype, device=dev)
+    cfg = KernelConfig(n_tile=args.n_tile, group_blocks=args.group_blocks, schedule=args.schedule,
+                       band_rows=args.band_rows)
     parts = ("wt_values", "dx", "dw")
 
     def part(name):
         if name == "wt_values":
             transpose_values(w, wt)
         elif name == "dx":
-            sparse_linear(dy, wt.matrix, out=dx)
+            sparse_linear(dy, wt.matrix, out=dx, config=cfg)
         else:
             sparse_linear_weight_grad(dy, x, w, wt, out_dtype=spec.dtype)
 
@@ -562,12 +564,13 @@ def run_backward(args) -> None:
         "data": "synthetic (seeded, generated on device)",
         "config": {"workload": spec.name, "m": spec.m, "k": spec.k, "batch": spec.n, "block": spec.block,
                    "sparsity": spec.sparsity, "nnzb": w.nnzb, "parts_ms": ms,
+                   "dx_plan": describe(wt.matrix, spec.n, linear=True, config=cfg),
                    "l2": "flushed before every part (256 MiB write, untimed)"},
         "roofline": {"bound": "tensor", "kernel": "bsr_sddmm_tc (dW)", "achieved": sdd_tflops, "peak": tpeak,
                      "unit": "TFLOP/s", "frac": sdd_tflops / tpeak, "traffic": None, "peak_kind": peak_kind},
         "cpu_baseline": None,
         # values refresh 1, dX per its plan, dW: stack list + SDDMM 2
-        "gpu_launches": args.steps * (1 + describe(wt.matrix, spec.n, linear=True)["launches"] + 2),
+        "gpu_launches": args.steps * (1 + describe(wt.matrix, spec.n, linear=True, config=cfg)["launches"] + 2),
         "clocks": sampler.summary(),
     }
     print(json.dumps(line), flush=True)

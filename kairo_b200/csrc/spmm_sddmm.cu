@@ -9,16 +9,18 @@
 // Y = X @ W.T restricted to W's nonzero blocks.
 //
 // Work.  Blocks are visited by block-column j (the transposed structure from
-// kairo_bsr_transpose), in stacks of S = 128 / bm blocks of one column.  A
-// stack shares its X panel, so X (the larger operand) is read about once;
-// the dY panels of all block-rows are reused from L2.  One stack is one MMA
-// tile: M = S * bm rows (the stacked dY panels, transposed), N = bk, K = the
-// batch, streamed in slabs of KB rows:
+// kairo_bsr_transpose).  A work item is up to U stacks of S = 128 / bm
+// blocks of one column, all sharing one X panel: every batch slab loads the
+// item's dY boxes and ONE X box, so the L2 -> SM gathers (which bound this
+// kernel) are 1 + 1/(S*U) boxes per block instead of 1 + 1/S.  One stack
+// is one MMA tile: M = S * bm rows (the stacked dY panels, transposed),
+// N = bk, K = the batch, streamed in slabs of KB rows:
 //   operand A = S dY boxes (bm columns x KB rows each), MN-major;
 //   operand B = the X box  (bk columns x KB rows),      MN-major;
-//   D in TMEM = 128 lanes (block rows of the S blocks) x bk fp32 columns.
-// Rows of a stack beyond its last block repeat that block and are not
-// written.
+//   D in TMEM = 128 lanes (block rows of the S blocks) x bk fp32 columns,
+//               one accumulator per stack, two sets of U (512 columns).
+// Rows of a stack beyond the item's last block repeat that block and are
+// not written.
 //
 // Roles (192 threads, persistent): warp 0 TMA producer, warp 1 TMEM
 // allocator + MMA issuer, warps 2..5 epilogue (TMEM -> dW).  Every mbarrier
@@ -40,11 +42,12 @@ namespace kairo {
 namespace {
 
 constexpr int kSddKB = 64;          // batch rows per pipeline stage
+constexpr int kSddU = 4;            // stacks (MMA tiles) per work item, sharing the X box
 constexpr int kItemScanThreads = 1024;
 
 struct SddItem {
   int32_t q0;    // first transposed position of the stack
-  int32_t cnt;   // blocks in the stack (1..S)
+  int32_t cnt;   // blocks in the item (1..S*U)
   int32_t col;   // block-column j
   int32_t pad;
 };
@@ -67,8 +70,8 @@ size_t sdd_ws_bytes(int64_t nnzb, int64_t nbc, int S) {
   return kWorkspaceHeaderBytes + static_cast<size_t>(max_items) * sizeof(SddItem);
 }
 
-// One CTA: for every block-column, ceil(len / S) stacks; exclusive scan of
-// the stack counts, then the stack list.
+// One CTA: for every block-column, ceil(len / S) items of up to S blocks;
+// exclusive scan of the item counts, then the item list.
 __global__ void __launch_bounds__(kItemScanThreads) k_sdd_items(const int32_t* __restrict__ row_ptr_t, int32_t nbc,
                                                                 int S, SddItem* __restrict__ items, int* nitems) {
   __shared__ int warp_sums[kItemScanThreads / 32];
@@ -162,19 +165,22 @@ __device__ __forceinline__ void store_row16<__nv_bfloat16>(__nv_bfloat16* dst, c
   store_row16_16bit(dst, v);
 }
 
-// tcgen05 kernel for bm = bk = 64 (S = 2 blocks per stack).
+// tcgen05 kernel for bm = bk = 64 (S = 2 blocks per stack, U stacks per item).
 template <int IN_FMT, typename TOut>
 __global__ void __launch_bounds__(kThreads, 1)
     bsr_sddmm_tc_kernel(const __grid_constant__ CUtensorMap tmap_dy, const __grid_constant__ CUtensorMap tmap_x,
                         const SddArgs args) {
   constexpr int BS = 64;
   constexpr int S = 128 / BS;
+  constexpr int U = kSddU;
+  constexpr int SU = S * U;                          // blocks per item
   constexpr int KB = kSddKB;
   constexpr int BOX_BYTES = BS * KB * 2;             // one 64-column box of KB rows
-  constexpr int STAGE_BYTES = (S + 1) * BOX_BYTES;   // S dY boxes, then the X box
-  constexpr uint32_t TX_BYTES = STAGE_BYTES;
+  constexpr int STAGE_BYTES = (SU + 1) * BOX_BYTES;  // SU dY boxes, then the X box
   constexpr uint32_t IDESC = ptx::make_idesc_f16(IN_FMT, 1u, 1u, 128u, BS);
-  constexpr uint32_t TMEM_COLS = 2 * BS;             // two accumulators of BS columns
+  constexpr uint32_t SET_COLS = U * BS;              // one accumulator set: U stacks
+  constexpr uint32_t TMEM_COLS = 2 * SET_COLS;       // two sets (512 columns)
+  static_assert(TMEM_COLS <= 512, "TMEM budget");
   constexpr uint32_t KSTEP16 = (16 * 128) >> 4;      // 16 batch rows of a 128-byte atom row
 
   extern __shared__ uint8_t smem_raw[];
@@ -230,9 +236,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool alive = true;
     for (int t = blockIdx.x; t < nitems && alive; t += G) {
       const SddItem it = args.items[t];
-      // lane s < S: block-row of stack slot s (the last block repeated)
+      const int nst = (it.cnt + S - 1) / S;  // stacks in this item
+      const uint32_t tx = static_cast<uint32_t>(nst * S + 1) * BOX_BYTES;
+      // lane l < nst*S: block-row of item slot l (the last block repeated)
       int row = 0;
-      if (lane < S) {
+      if (lane < nst * S) {
         const int q = it.q0 + min(lane, it.cnt - 1);
         row = (q >= 0 && q < args.nnzb) ? __ldg(args.col_idx_t + q) : -1;
         if (row < 0 || row >= args.nbr) {
@@ -250,9 +258,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) issued[sidx] = static_cast<int>(sph) + 1;
         uint8_t* st = smem + sidx * STAGE_BYTES;
         const int y = slab * KB;
-        ptx::mbar_expect_tx_if(lane == 0 ? 1u : 0u, &full[sidx], TX_BYTES);
-        ptx::tma_load_2d_if(lane < S ? 1u : 0u, st + lane * BOX_BYTES, &tmap_dy, row * BS, y, &full[sidx], pol_dy);
-        ptx::tma_load_2d_if(lane == S ? 1u : 0u, st + S * BOX_BYTES, &tmap_x, it.col * BS, y, &full[sidx], pol_x);
+        ptx::mbar_expect_tx_if(lane == 0 ? 1u : 0u, &full[sidx], tx);
+        ptx::tma_load_2d_if(lane < nst * S ? 1u : 0u, st + lane * BOX_BYTES, &tmap_dy, row * BS, y, &full[sidx],
+                            pol_dy);
+        ptx::tma_load_2d_if(lane == 31 ? 1u : 0u, st + SU * BOX_BYTES, &tmap_x, it.col * BS, y, &full[sidx], pol_x);
         __syncwarp();
         ptx::mbar_arrive_if(lane == 0 ? 1u : 0u, &full[sidx]);
         if (++sidx == ST) {
@@ -267,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t sbase = ptx::smem_u32(smem);
     // A: S dY boxes side by side along M (atom stride BOX_BYTES); B: the X box.
     const uint64_t adesc0 = ptx::make_smem_desc(sbase, BOX_BYTES, 1024, 2u);
-    const uint64_t bdesc0 = ptx::make_smem_desc(sbase + S * BOX_BYTES, BOX_BYTES, 1024, 2u);
+    const uint64_t bdesc0 = ptx::make_smem_desc(sbase + SU * BOX_BYTES, BOX_BYTES, 1024, 2u);
     const uint32_t a_lo0 = static_cast<uint32_t>(adesc0), a_hi = static_cast<uint32_t>(adesc0 >> 32);
     const uint32_t b_lo0 = static_cast<uint32_t>(bdesc0), b_hi = static_cast<uint32_t>(bdesc0 >> 32);
     constexpr uint32_t STAGE16 = STAGE_BYTES >> 4;
@@ -277,11 +286,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t aphase = 0;
     bool alive = true;
     for (int t = blockIdx.x; t < nitems && alive; t += G) {
+      const int nst = (args.items[t].cnt + S - 1) / S;
       int ok = ptx::wait_parity(&tempty[slot], aphase ^ 1u, abort_flag, args.err, kTagTmemEmpty, kWaitCycles);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       ptx::tc_fence_after();
-      const uint32_t d = tmem_base + static_cast<uint32_t>(slot * BS);
+      const uint32_t d = tmem_base + static_cast<uint32_t>(slot) * SET_COLS;
       for (int slab = 0; slab < nslabs; ++slab) {
         ok = ptx::wait_parity(&full[sidx], sph, abort_flag, args.err, kTagFull, kWaitCycles);
         ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -290,10 +300,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const uint32_t s16 = static_cast<uint32_t>(sidx) * STAGE16;
+        for (int u = 0; u < nst; ++u) {
+          const uint32_t u16 = static_cast<uint32_t>(u * S * BOX_BYTES) >> 4;
 #pragma unroll
-        for (int kk = 0; kk < KB / 16; ++kk) {
-          ptx::mma_f16_ss_if(leader, d, a_lo0 + s16 + kk * KSTEP16, a_hi, b_lo0 + s16 + kk * KSTEP16, b_hi, IDESC,
-                             (slab > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < KB / 16; ++kk) {
+            ptx::mma_f16_ss_if(leader, d + static_cast<uint32_t>(u * BS), a_lo0 + s16 + u16 + kk * KSTEP16, a_hi,
+                               b_lo0 + s16 + kk * KSTEP16, b_hi, IDESC, (slab > 0 || kk > 0) ? 1u : 0u);
+          }
         }
         ptx::mma_commit_if(leader, &empty[sidx]);
         if (++sidx == ST) {
@@ -313,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 2 && warp <= 5) {
     // ------------------------------------------------------------ epilogue
     const int qtr = warp & 3;
-    const int e = qtr * 32 + lane;  // TMEM lane: row e % BS of stack slot e / BS
+    const int e = qtr * 32 + lane;  // TMEM lane: row e % BS of slot e / BS of a stack
     const int sslot = e / BS, r = e % BS;
     const uint32_t lane_addr = static_cast<uint32_t>(qtr * 32) << 16;
     int slot = 0;
@@ -324,19 +337,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (epi_any(!ok)) break;
       ptx::tc_fence_after();
-      int p = -1;
-      if (sslot < it.cnt) {
-        const int q = it.q0 + sslot;
-        p = (q >= 0 && q < args.nnzb) ? __ldg(args.perm_t + q) : -1;
-        if (p >= args.nnzb) p = -1;
-      }
-      TOut* dst = p >= 0 ? static_cast<TOut*>(args.dblocks) + (static_cast<int64_t>(p) * BS + r) * BS : nullptr;
+      const int nst = (it.cnt + S - 1) / S;
+      for (int u = 0; u < nst; ++u) {
+        const int bi = u * S + sslot;  // block of the item in this lane's TMEM rows
+        int p = -1;
+        if (bi < it.cnt) {
+          const int q = it.q0 + bi;
+          p = (q >= 0 && q < args.nnzb) ? __ldg(args.perm_t + q) : -1;
+          if (p >= args.nnzb) p = -1;
+        }
+        TOut* dst = p >= 0 ? static_cast<TOut*>(args.dblocks) + (static_cast<int64_t>(p) * BS + r) * BS : nullptr;
+        const uint32_t cols = static_cast<uint32_t>(slot) * SET_COLS + static_cast<uint32_t>(u * BS);
 #pragma unroll
-      for (int c0 = 0; c0 < BS; c0 += 16) {
-        float v[16];
-        ptx::tmem_ld16(tmem_base + lane_addr + static_cast<uint32_t>(slot * BS + c0), v);
-        ptx::tmem_wait_ld();
-        if (dst) store_row16<TOut>(dst + c0, v);
+        for (int c0 = 0; c0 < BS; c0 += 16) {
+          float v[16];
+          ptx::tmem_ld16(tmem_base + lane_addr + cols + static_cast<uint32_t>(c0), v);
+          ptx::tmem_wait_ld();
+          if (dst) store_row16<TOut>(dst + c0, v);
+        }
       }
       ptx::tc_fence_before();
       __syncwarp();
@@ -512,7 +530,7 @@ extern "C" kairo_status kairo_bsr_sddmm(const kairo_bsr* a, const int32_t* row_p
     }
   }
   const int nbc = static_cast<int>(ceil_div64(a->cols, a->bk));
-  k_sdd_items<<<1, kItemScanThreads, 0, s>>>(row_ptr_t, nbc, 2, w.items, w.nitems);
+  k_sdd_items<<<1, kItemScanThreads, 0, s>>>(row_ptr_t, nbc, 2 * kSddU, w.items, w.nitems);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch of the SDDMM item kernel");
   const CUtensorMapDataType dt =
@@ -524,7 +542,7 @@ extern "C" kairo_status kairo_bsr_sddmm(const kairo_bsr* a, const int32_t* row_p
   st = make_map_2d(&map_x, x, dt, 2, static_cast<uint64_t>(a->cols), static_cast<uint64_t>(n),
                    static_cast<uint64_t>(ldx), 64, kSddKB, "X");
   if (st) return st;
-  constexpr int stage_bytes = 3 * 64 * kSddKB * 2;
+  constexpr int stage_bytes = (2 * kSddU + 1) * 64 * kSddKB * 2;
   const int budget = kMaxSmem - 1024 - 1024;
   const int stages = std::min(8, budget / stage_bytes);
   SddArgs args{};
@@ -543,7 +561,7 @@ extern "C" kairo_status kairo_bsr_sddmm(const kairo_bsr* a, const int32_t* row_p
   e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem));
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
-  const int64_t max_items = a->nnzb / 2 + nbc;
+  const int64_t max_items = a->nnzb / (2 * kSddU) + nbc;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(device_sm_count(current_device()), max_items)));
   fn<<<grid, kThreads, smem, s>>>(map_dy, map_x, args);
   e = cudaGetLastError();

@@ -43,11 +43,14 @@ def _scratch(nbytes: int, device: torch.device) -> Tensor:
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
 
 
-def bsr_transpose(a: BlockSparseMatrix, *, check: bool = False) -> TransposedBsr:
-    """W^T on the device (structure and transposed blocks), asynchronously.
+def bsr_transpose(a: BlockSparseMatrix, *, check: bool = False, row_hint: bool = True) -> TransposedBsr:
+    """W^T on the device (structure and transposed blocks).
 
-    ``check=True`` synchronises and raises KairoDeviceError on an invalid
-    index or a block-column longer than 16384 blocks."""
+    ``row_hint`` reads W^T's longest block-row back from the device (one
+    synchronisation) into ``max_row_blocks``, the hint the SpMM scheduler
+    uses to pick the band schedule; with ``row_hint=False`` the call is
+    asynchronous.  ``check=True`` synchronises and raises KairoDeviceError
+    on an invalid index or a block-column longer than 16384 blocks."""
     _require_cuda(a.blocks, a.row_ptr, op="bsr_transpose")
     m, k = a.shape
     bm, bk = a.block_size
@@ -68,7 +71,13 @@ def bsr_transpose(a: BlockSparseMatrix, *, check: bool = False) -> TransposedBsr
                                            ws.data_ptr(), ws.numel(), _lib.stream_handle(dev)), "bsr_transpose")
         if check:
             _lib.raise_on_device_error(ws)
-    wt = BlockSparseMatrix(row_ptr=row_ptr_t, col_idx=col_idx_t, blocks=blocks_t, shape=(k, m), block_size=(bk, bm))
+        longest = 0
+        if row_hint and a.nnzb:
+            # the bucket sort leaves the longest bucket (W^T row) in the
+            # workspace header's second flag word
+            longest = int(ws[64:72].view(torch.int32)[1].item())
+    wt = BlockSparseMatrix(row_ptr=row_ptr_t, col_idx=col_idx_t, blocks=blocks_t, shape=(k, m), block_size=(bk, bm),
+                           max_row_blocks=longest)
     return TransposedBsr(matrix=wt, perm=perm_t)
 
 

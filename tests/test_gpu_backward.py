@@ -61,6 +61,7 @@ def test_transpose_bit_exact(case):
     stored = w.blocks if w.blk_idx is None else w.blocks[w.blk_idx.long()]
     assert torch.equal(t.matrix.blocks, stored[pt.to(DEV).long()].transpose(1, 2))
     assert t.matrix.shape == (k, m) and t.matrix.block_size == (bs, bs)
+    assert t.matrix.max_row_blocks == int((rpt[1:] - rpt[:-1]).max())
 
 
 def test_transpose_unaligned_blocks():

@@ -143,9 +143,10 @@ def _uniform_rows_matrix(nbr, nbc, per_row, bs, max_row_blocks):
 
 
 def test_schedule_choice():
-    """AUTO picks the band schedule only when a chunk has fewer block-rows than
-    twice the SMs (the row-split schedule would cut most rows), with enough
-    items and a row-length hint showing similar rows; otherwise rows."""
+    """AUTO picks the band schedule when a chunk has fewer block-rows than
+    twice the SMs (the row-split schedule would cut most rows) or the block
+    grid is at least 10 % dense, with enough items and a row-length hint
+    showing similar rows; otherwise rows."""
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     # many short rows (the 262144^2 case): rows
     a = _uniform_rows_matrix(1024, 8192, 41, 32, max_row_blocks=41)
@@ -164,6 +165,10 @@ def test_schedule_choice():
     a2 = _uniform_rows_matrix(1024, 512, 41, 32, max_row_blocks=41)
     plan2 = describe(a2, 1024)
     assert plan2["schedule"] == "rows" and (plan2["stages"], plan2["group_blocks"]) == (3, 4)
+    # many rows on a dense block grid (the transposed linear-layer weight,
+    # 20 % of 512 x 128 blocks): bands
+    c = _uniform_rows_matrix(512, 128, 26, 64, max_row_blocks=26)
+    assert describe(c, 8192)["schedule"] == "bands"
 
 
 def test_build_reports_longest_row():
