@@ -576,6 +576,88 @@ def run_backward(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- block pruning
+
+def run_prune(args) -> None:
+    """The linear layer's mask generator as a step: block L2 norms of the
+    dense weight (8192 x 32768 bf16, 64 x 64 blocks) and the top 20 % of the
+    65536 block scores, indices ascending (block_magnitude_mask).  HBM-bound:
+    the weight is read once."""
+    from kairo_b200.pruning import block_magnitude_mask, block_norms, topk_indices
+
+    rank, world, local = dist_env()
+    if world > 1:
+        raise SystemExit("--op prune runs on one GPU")
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    m, k, bs, keep = 8192, 32768, 64, 0.2
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    w = (torch.randn(m, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    nblocks = (m // bs) * (k // bs)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ev = []
+    sampler = ClockSampler(dev)
+    with sampler:
+        for i in range(args.warmup + args.steps):
+            flush.zero_()
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record(stream)
+            scores = block_norms(w, bs)
+            e1.record(stream)
+            idx = topk_indices(scores, int(nblocks * keep))
+            e2.record(stream)
+            if i >= args.warmup:
+                ev.append((e0, e1, e2))
+        torch.cuda.synchronize()
+    norms_ms = sum(a.elapsed_time(b) for a, b, _ in ev) / args.steps
+    topk_ms = sum(b.elapsed_time(c) for _, b, c in ev) / args.steps
+    ms = norms_ms + topk_ms
+    mask = block_magnitude_mask(w, bs, keep)  # the public call, checked against the two parts
+    assert torch.equal(mask.indices[0] * (k // bs) + mask.indices[1], idx)
+    nbytes = m * k * 2 + nblocks * 4
+    peaks, peak_kind = measured_peaks()
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    achieved = nbytes / (norms_ms / 1e3) / 1e9
+
+    cpu = None
+    if not args.no_cpu:
+        # The reference's rule with torch on the host (per-block norm, topk,
+        # sort) on the first 512 block-columns' worth of rows: 1/16 of W.
+        hw = w[: m // 16].float().cpu()
+        t0 = time.perf_counter()
+        sc = hw.view(m // 16 // bs, bs, k // bs, bs).pow(2).sum(dim=(1, 3)).sqrt()
+        torch.topk(sc.reshape(-1), int(sc.numel() * keep)).indices.sort()
+        dt = time.perf_counter() - t0
+        cpu = {"value": (m // 16) * k * 2 / dt / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+               "kind": "port", "sample": f"rows 0..{m // 16 - 1} of the weight (1/16), torch on the host"}
+    line = {
+        "metric": "block_prune_weight_gbs",
+        "value": m * k * 2 / (ms / 1e3) / 1e9,
+        "unit": "GB/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded, generated on device)",
+        "config": {"workload": "linear-layer mask: top 20 % of 64x64 blocks of 8192x32768 bf16", "m": m, "k": k,
+                   "block": bs, "keep": keep, "parts_ms": {"block_norms": norms_ms, "topk": topk_ms},
+                   "l2": "flushed before every step (256 MiB write, untimed)"},
+        "roofline": {"bound": "hbm", "kernel": "block norms", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "traffic": None, "peak_kind": peak_kind},
+        "cpu_baseline": cpu,
+        "gpu_launches": args.steps * 13,  # block norms 1; top-k: init, 4 x (histogram, pick), count, scan, write
+        "clocks": sampler.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 # ---------------------------------------------------------------- embedding ops
 
 EMB_WORKLOADS = {
@@ -791,8 +873,9 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=3.0)
-    ap.add_argument("--op", choices=("spmm", "backward", "gather", "scatter"), default="spmm",
+    ap.add_argument("--op", choices=("spmm", "backward", "prune", "gather", "scatter"), default="spmm",
                     help="spmm (default): the block-sparse SpMM; backward: the linear layer's dX and dW; "
+                         "prune: block norms + top-k of the linear layer's weight; "
                          "gather/scatter: the masked embedding ops")
     ap.add_argument("--emb-workload", choices=sorted(EMB_WORKLOADS), default="emb_large")
     args = ap.parse_args()
@@ -803,6 +886,8 @@ def main() -> None:
             raise SystemExit("--impl reference times the SpMM path only")
         if args.op == "backward":
             run_backward(args)
+        elif args.op == "prune":
+            run_prune(args)
         else:
             run_embedding(args)
     elif args.impl == "reference":

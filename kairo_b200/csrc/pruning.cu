@@ -65,6 +65,47 @@ __global__ void __launch_bounds__(kNormThreads) k_dense_block_norms(const T* __r
   }
 }
 
+// Sum of squares of the VE elements packed in a 16-byte vector.
+template <typename T>
+__device__ __forceinline__ float sumsq16(const uint4& v) {
+  const T* e = reinterpret_cast<const T*>(&v);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < static_cast<int>(16 / sizeof(T)); ++i) {
+    const float f = to_f(e[i]);
+    s = fmaf(f, f, s);
+  }
+  return s;
+}
+
+// The same with 16-byte loads, for whole blocks whose rows start on 16-byte
+// boundaries (bk and lda multiples of the vector, aligned base): a block row
+// is vpr vectors, a warp covers 32 / vpr rows per step, so every step reads
+// whole 16-byte-aligned row segments, coalesced.
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads) k_dense_block_norms_vec(const T* __restrict__ a, int64_t lda,
+                                                                        int32_t bm, int32_t bk, int64_t nbc,
+                                                                        int64_t nblocks, float* __restrict__ norms) {
+  constexpr int VE = 16 / sizeof(T);
+  const int lane = threadIdx.x & 31;
+  const int vpr = bk / VE;  // vectors per block row (a power of two, <= 32)
+  const int nvec = bm * vpr;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (kNormThreads / 32);
+  for (int64_t b = static_cast<int64_t>(blockIdx.x) * (kNormThreads / 32) + (threadIdx.x >> 5); b < nblocks;
+       b += warps) {
+    const int64_t i = b / nbc, j = b - i * nbc;
+    const T* base = a + i * bm * lda + j * bk;
+    float s = 0.f;
+#pragma unroll 4
+    for (int e = lane; e < nvec; e += 32) {
+      const int r = e / vpr, v = e - r * vpr;
+      s += sumsq16<T>(*reinterpret_cast<const uint4*>(base + r * lda + v * VE));
+    }
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (lane == 0) norms[b] = sqrtf(s);
+  }
+}
+
 // One warp per BSR position: norms[p] of block stored(p).
 template <typename T>
 __global__ void __launch_bounds__(kNormThreads) k_bsr_block_norms(const T* __restrict__ blocks,
@@ -79,9 +120,16 @@ __global__ void __launch_bounds__(kNormThreads) k_bsr_block_norms(const T* __res
     float acc = 0.f;
     if (s >= 0 && s < nstored) {
       const T* blk = blocks + s * elems;
-      for (int e = lane; e < elems; e += 32) {
-        const float v = to_f(blk[e]);
-        acc = fmaf(v, v, acc);
+      constexpr int VE = 16 / sizeof(T);
+      if (elems % VE == 0 && (reinterpret_cast<uintptr_t>(blk) & 15u) == 0) {
+        const uint4* b4 = reinterpret_cast<const uint4*>(blk);
+#pragma unroll 4
+        for (int e = lane; e < elems / VE; e += 32) acc += sumsq16<T>(b4[e]);
+      } else {
+        for (int e = lane; e < elems; e += 32) {
+          const float v = to_f(blk[e]);
+          acc = fmaf(v, v, acc);
+        }
       }
     }
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -307,6 +355,31 @@ extern "C" kairo_status kairo_block_norms(const void* a, int64_t m, int64_t k, i
   if (!a || !norms) return fail(KAIRO_STATUS_INVALID_VALUE, "null pointer argument");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int g = grid_over(nb, kNormThreads / 32);
+  const int ve = dtype == KAIRO_DTYPE_F32 ? 4 : 8;
+  const bool pow2 = bk >= ve && (bk / ve) <= 32 && ((bk / ve) & (bk / ve - 1)) == 0;
+  const bool vec = pow2 && bk % ve == 0 && lda % ve == 0 && m % bm == 0 && k % bk == 0 &&
+                   (reinterpret_cast<uintptr_t>(a) & 15u) == 0;
+  if (vec) {
+    switch (dtype) {
+      case KAIRO_DTYPE_F32:
+        k_dense_block_norms_vec<float><<<g, kNormThreads, 0, s>>>(static_cast<const float*>(a), lda, bm, bk, nbc, nb,
+                                                                  norms);
+        break;
+      case KAIRO_DTYPE_F16:
+        k_dense_block_norms_vec<__half><<<g, kNormThreads, 0, s>>>(static_cast<const __half*>(a), lda, bm, bk, nbc,
+                                                                   nb, norms);
+        break;
+      case KAIRO_DTYPE_BF16:
+        k_dense_block_norms_vec<__nv_bfloat16><<<g, kNormThreads, 0, s>>>(static_cast<const __nv_bfloat16*>(a), lda,
+                                                                          bm, bk, nbc, nb, norms);
+        break;
+      default:
+        return fail(KAIRO_STATUS_INVALID_VALUE, "unknown dtype");
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, "launch of the block-norm kernel");
+    return KAIRO_STATUS_SUCCESS;
+  }
   switch (dtype) {
     case KAIRO_DTYPE_F32:
       k_dense_block_norms<float><<<g, kNormThreads, 0, s>>>(static_cast<const float*>(a), m, k, lda, bm, bk, nbc, nb,
