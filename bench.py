@@ -116,6 +116,20 @@ class ClockSampler:
                 "samples": len(sms)}
 
 
+def l2_gather_peak(flush: torch.Tensor) -> float | None:
+    """L2 -> SM bulk-copy ceiling of this GPU in GB/s (kairo_gather_probe on
+    a 32 MiB, L2-resident slice; 16 KiB copies, the size of a gathered
+    panel), measured live.  None if the probe fails."""
+    import ctypes
+
+    from kairo_b200 import _lib
+
+    out = ctypes.c_double(0.0)
+    st = _lib.lib().kairo_gather_probe(flush.data_ptr(), 32 << 20, 16384, 400, ctypes.byref(out),
+                                       _lib.stream_handle(flush.device))
+    return out.value if st == 0 else None
+
+
 def load_traffic(workload: str) -> float | None:
     """DRAM bytes per launch of the SpMM kernel for the full single-GPU
     workload, from the committed ncu summary (profiles/traffic_<workload>.txt)."""
@@ -302,6 +316,7 @@ def run_ours(args) -> None:
         dist.barrier()
     torch.cuda.synchronize()
     per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]  # ms
+    l2_peak = l2_gather_peak(flush)
     total_ms = sum(per_step)
     t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
     if world > 1:
@@ -388,6 +403,10 @@ def run_ours(args) -> None:
                 "bytes_definition": "canonical: A blocks + int32 indices + gathered B panel per block + C",
                 "strict_frac": local_strict / (my_ms / 1e3) / 1e9 / hbm,
                 "tensor_frac": local_flop / (my_ms / 1e3) / 1e12 / bf16_peak,
+                # The gathered panels are served by L2: the canonical bytes
+                # against this GPU's measured L2 -> SM bulk-copy ceiling.
+                "l2_gather_peak_gbs": l2_peak,
+                "l2_frac": (achieved / l2_peak) if l2_peak else None,
             },
             "cpu_baseline": cpu,
             "e2e": e2e,

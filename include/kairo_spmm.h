@@ -318,6 +318,17 @@ KAIRO_API kairo_status kairo_sparse_scatter_grad(const void* grad_output, kairo_
 KAIRO_API kairo_status kairo_sparse_scatter_grad_workspace_size(int64_t nactive, int64_t nbatch, size_t* bytes);
 
 /* ------------------------------------------------------------------------
+ * Diagnostics (no counterpart in the reference): the rate at which the SMs
+ * pull bulk copies of `load_bytes` (a multiple of 16 dividing 32768) from
+ * pseudo-random offsets of `buffer` into shared memory, in GB/s summed over
+ * all SMs.  With a buffer smaller than the L2 this is the L2 -> SM gather
+ * ceiling that bounds the tcgen05 kernels (one gathered panel per block).
+ * Runs one CTA per SM on `stream` and synchronises it.
+ * ---------------------------------------------------------------------- */
+KAIRO_API kairo_status kairo_gather_probe(const void* buffer, size_t buffer_bytes, uint32_t load_bytes,
+                                          int32_t iterations, double* gb_per_s, void* stream);
+
+/* ------------------------------------------------------------------------
  * Dense A (M x K, leading dimension lda) -> tiles (num_tiles, tile, tile) in
  * COO order, zero-padding tiles that cross the right/bottom edge.  Replaces
  * the per-tile host loop of _dense_to_block_sparse (kairo/ops/spmm.py:16-55).

@@ -166,6 +166,7 @@ _SIGNATURES = {
     "kairo_sparse_scatter_grad": (c_int32, [c_void_p, c_int32, c_void_p, c_int64, c_void_p, c_int64, c_int64,
                                             c_int64, c_void_p, c_void_p, c_size_t, c_void_p]),
     "kairo_sparse_scatter_grad_workspace_size": (c_int32, [c_int64, c_int64, POINTER(c_size_t)]),
+    "kairo_gather_probe": (c_int32, [c_void_p, c_size_t, c_uint32, c_int32, POINTER(ctypes.c_double), c_void_p]),
     "kairo_dense_to_tiles": (c_int32, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int32,
                                        c_int32, c_void_p, c_void_p]),
     "kairo_acc_spmm_forward": (c_int32, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
