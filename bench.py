@@ -258,6 +258,10 @@ def run_ours(args) -> None:
     if world > 1:
         from datetime import timedelta
 
+        # NCCL's version banner goes to stdout, where the one JSON line of
+        # rank 0 must stand alone; keep warnings, unless more was asked for.
+        if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+            os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     spec = workload_spec(args)
     t0 = time.perf_counter()
