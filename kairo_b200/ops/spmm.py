@@ -110,6 +110,8 @@ def block_sparse_mm(
     B: Tensor,
     block_mask: SparseMask,
     tile_size: int = 16,
+    *,
+    out_dtype: torch.dtype | None = None,
 ) -> Tensor:
     """Block-sparse matrix multiply: C = blocksparse(A) @ B.
 
@@ -124,23 +126,28 @@ def block_sparse_mm(
         B: dense (K, N) matrix on the same device, same dtype as A.
         block_mask: SparseMask with tile-granular indices.
         tile_size: tile side length (default 16).
+        out_dtype: None (the reference's fp32 result), torch.float32, or A's
+            dtype: the fp32 accumulation rounded once.
     """
     M, K = A.shape
     K2, N = B.shape
     if K != K2:
         raise ValueError(f"Inner dimensions must match: A is ({M}, {K}), B is ({K2}, {N})")
     _require_cuda(A, B, op="block_sparse_mm")
+    if out_dtype not in (None, torch.float32, A.dtype):
+        raise TypeError("out_dtype must be None, torch.float32 or A's dtype")
     A_tiles, tile_row_ids, tile_col_ids = _dense_to_block_sparse(A, block_mask, tile_size)
     num_tiles = A_tiles.shape[0]
     if num_tiles == 0:
-        return torch.zeros(M, N, dtype=A.dtype, device=A.device)
-    return _C.acc_spmm_forward(
+        return torch.zeros(M, N, dtype=out_dtype or A.dtype, device=A.device)
+    C = _C.acc_spmm_forward(
         A_tiles.contiguous(),
         tile_row_ids.contiguous(),
         tile_col_ids.contiguous(),
         B.contiguous(),
         M, K, N, num_tiles, tile_size, tile_size,
     )
+    return C if out_dtype in (None, torch.float32) else C.to(out_dtype)
 
 
 def bsr_from_tiles(

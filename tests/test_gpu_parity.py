@@ -238,6 +238,24 @@ def test_acc_spmm_forward_fp32_reference_case():
     assert torch.allclose(cpu, out.cpu(), atol=1e-3)
 
 
+def test_block_sparse_mm_out_dtype():
+    """out_dtype=None / float32 give the fp32 product; A's dtype rounds it once."""
+    M, K, N, tile = 128, 96, 64, 32
+    g = torch.Generator().manual_seed(8)
+    A = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    B = torch.randn(K, N, generator=g).to(torch.bfloat16)
+    keep = torch.rand(M // tile, K // tile, generator=g) < 0.6
+    r, c = keep.nonzero(as_tuple=True)
+    mask = SparseMask(torch.stack([r, c]).cuda(), torch.ones(r.numel()).cuda(), (M // tile, K // tile), 0.4)
+    c32 = block_sparse_mm(A.cuda(), B.cuda(), mask, tile_size=tile)
+    assert c32.dtype == torch.float32
+    assert torch.equal(block_sparse_mm(A.cuda(), B.cuda(), mask, tile_size=tile, out_dtype=torch.float32), c32)
+    cb = block_sparse_mm(A.cuda(), B.cuda(), mask, tile_size=tile, out_dtype=torch.bfloat16)
+    assert cb.dtype == torch.bfloat16 and torch.equal(cb, c32.to(torch.bfloat16))
+    with pytest.raises(TypeError):
+        block_sparse_mm(A.cuda(), B.cuda(), mask, tile_size=tile, out_dtype=torch.float16)
+
+
 def test_empty_and_zero_rows():
     spec = WorkloadSpec("t", torch.float16, 256, 256, 128, 32, 0.97)
     p = generate(spec, seed=1)
