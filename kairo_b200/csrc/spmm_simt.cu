@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(kSimtCols)
 // unrolled) before the FMAs.  The groups' partial sums are added in group
 // order at the end, so the result is deterministic.
 template <int BM_CAP, int BK, int KS, typename TIn>
-__global__ void __launch_bounds__(kSimtCols * KS)
+__global__ void __launch_bounds__(kSimtCols * KS, KS >= 4 ? 2 : 1)
     bsr_spmm_simt_rows_kernel(const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx,
                               const int32_t* __restrict__ blk_idx, const TIn* __restrict__ blocks,
                               const TIn* __restrict__ b, int64_t ldb, float* __restrict__ c, int64_t ldc, int32_t m,
@@ -115,12 +115,19 @@ __global__ void __launch_bounds__(kSimtCols * KS)
   const int p_begin = row_ptr[i];
   const int p_end = row_ptr[i + 1];
   const int blk_elems = bm * BK;
+  const bool full_rows = bm == BM_CAP;  // the common case: index math by shifts
   for (int c0 = p_begin; c0 < p_end; c0 += chunk_cap) {
     const int cn = min(chunk_cap, p_end - c0);
     __syncthreads();  // the previous chunk has been consumed
     for (int e = threadIdx.x; e < cn * blk_elems; e += blockDim.x) {
-      const int j = e / blk_elems;
-      const int rem = e - j * blk_elems;
+      int j, rem;
+      if (full_rows) {
+        j = e / BLK_F;
+        rem = e - j * BLK_F;
+      } else {
+        j = e / blk_elems;
+        rem = e - j * blk_elems;
+      }
       const int r = rem / BK, kk = rem - r * BK;
       const int64_t blk = blk_idx ? static_cast<int64_t>(blk_idx[c0 + j]) : static_cast<int64_t>(c0 + j);
       float v = 0.f;
@@ -138,8 +145,14 @@ __global__ void __launch_bounds__(kSimtCols * KS)
         }
         const int64_t k0 = static_cast<int64_t>(cb) * BK;
         float bv[BK];
+        const TIn* bp = b + k0 * ldb + col;
+        if (k0 + BK <= k) {
 #pragma unroll
-        for (int kk = 0; kk < BK; ++kk) bv[kk] = (k0 + kk < k) ? to_f32(b[(k0 + kk) * ldb + col]) : 0.f;
+          for (int kk = 0; kk < BK; ++kk) bv[kk] = to_f32(bp[kk * ldb]);
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < BK; ++kk) bv[kk] = (k0 + kk < k) ? to_f32(bp[kk * ldb]) : 0.f;
+        }
         const float4* a4 = reinterpret_cast<const float4*>(sm + j * BLK_F);
 #pragma unroll
         for (int kk = 0; kk < BK; ++kk) {
