@@ -24,6 +24,7 @@ workload.  Other ranks exit without work.
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import csv
 import io
 import json
@@ -248,7 +249,7 @@ def run_ours(args) -> None:
     import torch.distributed as dist
 
     from kairo_b200.ops import KernelConfig, block_sparse_mm_bsr, bsr_from_tiles, describe
-    from kairo_b200.sharding import gather_rows, partition_rows, shard_bsr
+    from kairo_b200.sharding import column_range, gather_grid, grid_coords, partition_rows, shard_bsr
 
     rank, world, local = dist_env()
     if not torch.cuda.is_available():
@@ -267,31 +268,39 @@ def run_ours(args) -> None:
     t0 = time.perf_counter()
     problem = generate(spec, seed=args.seed, device=dev)
     a_full = bsr_from_tiles(problem.tiles, problem.row_ids, problem.col_ids, (spec.m, spec.k))
-    bounds = partition_rows(a_full.row_ptr, world)
-    a, shard = shard_bsr(a_full, rank, world, bounds)
+    # Ranks form a (row groups x column slices) grid: block-rows balanced by
+    # nonzero count within the row groups, C's columns (the batch rows of X
+    # in the linear layout) sliced; no collective on the compute path.
+    row_group, col_slice, row_groups, col_slices = grid_coords(rank, world, spec.n)
+    if args.row_shards_only:
+        row_group, col_slice, row_groups, col_slices = rank, 0, world, 1
+    bounds = partition_rows(a_full.row_ptr, row_groups)
+    a, shard = shard_bsr(a_full, row_group, row_groups, bounds)
+    c0, c1 = column_range(spec.n, col_slices, col_slice)
+    ncols = c1 - c0
     local_nnzb = a.nnzb
     local_rows = a.shape[0]
-    b = problem.b
+    linear = spec.layout == "linear"
+    b = problem.b[c0:c1] if linear else problem.b[:, c0:c1]
     cfg = KernelConfig(n_tile=args.n_tile, group_blocks=args.group_blocks, schedule=args.schedule,
                        band_rows=args.band_rows)
-    linear = spec.layout == "linear"
-    plan = describe(a, spec.n, linear=linear, config=cfg)
-    out_rows = local_rows
+    plan = describe(a, ncols, linear=linear, config=cfg)
     if linear:
         from kairo_b200.ops import sparse_linear
 
-        out = torch.empty(spec.n, local_rows, dtype=spec.out_dtype, device=dev)
+        out = torch.empty(ncols, local_rows, dtype=spec.out_dtype, device=dev)
 
         def step():
             sparse_linear(b, a, out=out, config=cfg)
     else:
-        out = torch.empty(out_rows, spec.n, dtype=torch.float32, device=dev)
+        out = torch.empty(local_rows, ncols, dtype=torch.float32, device=dev)
 
         def step():
             block_sparse_mm_bsr(a, b, out=out, config=cfg)
     torch.cuda.synchronize()
-    log(f"[rank {rank}] workload {spec.name}: shard rows {shard.row_begin}..{shard.row_end} of {a_full.nbr}, "
-        f"{local_nnzb} blocks, ready in {time.perf_counter() - t0:.1f}s")
+    log(f"[rank {rank}] workload {spec.name}: grid {row_groups}x{col_slices}, rows {shard.row_begin}..{shard.row_end} "
+        f"of {a_full.nbr}, columns {c0}..{c1} of {spec.n}, {local_nnzb} blocks, ready in "
+        f"{time.perf_counter() - t0:.1f}s")
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -332,15 +341,16 @@ def run_ours(args) -> None:
 
     peaks, peak_kind = measured_peaks()
     hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
-    local_flop = flops(spec, nnzb=local_nnzb)
-    local_canon = canonical_bytes(spec, nnzb=local_nnzb, nbr=a.nbr, m=local_rows)
-    local_strict = strict_bytes(spec, nnzb=local_nnzb, nbr=a.nbr, m=local_rows)
+    local_spec = dataclasses.replace(spec, n=ncols)
+    local_flop = flops(local_spec, nnzb=local_nnzb)
+    local_canon = canonical_bytes(local_spec, nnzb=local_nnzb, nbr=a.nbr, m=local_rows)
+    local_strict = strict_bytes(local_spec, nnzb=local_nnzb, nbr=a.nbr, m=local_rows)
     my_ms = total_ms / args.steps
     achieved = local_canon / (my_ms / 1e3) / 1e9
     traffic_full = load_traffic(spec.name)
     traffic = None
     if traffic_full is not None:
-        traffic = traffic_full * (local_nnzb / max(1, a_full.nnzb))
+        traffic = traffic_full * (local_nnzb / max(1, a_full.nnzb)) * (ncols / spec.n)
     bf16_peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
 
     # Optional replicated output (reported separately, not part of the step).
@@ -351,7 +361,7 @@ def run_ours(args) -> None:
         g0 = torch.cuda.Event(enable_timing=True)
         g1 = torch.cuda.Event(enable_timing=True)
         g0.record(stream)
-        gather_rows(out, bounds, shard.block_rows, spec.m)
+        gather_grid(out, bounds, shard.block_rows, spec.m, spec.n, row_groups, col_slices)
         g1.record(stream)
         torch.cuda.synchronize()
         gt = torch.tensor([g0.elapsed_time(g1)], dtype=torch.float64, device=dev)
@@ -389,7 +399,8 @@ def run_ours(args) -> None:
             "config": {
                 "workload": spec.name, "m": spec.m, "k": spec.k, "n": spec.n, "block": spec.block,
                 "sparsity": spec.sparsity, "nnzb": a_full.nnzb, "out_dtype": str(spec.out_dtype).replace("torch.", ""),
-                "parallelism": f"row-shard{world} (nnz-balanced block rows, B replicated)",
+                "parallelism": (f"grid {row_groups}x{col_slices} (nnz-balanced block-row groups x column slices "
+                                f"of B and C, B replicated)"),
                 "l2": "flushed before every step (256 MiB write, untimed)",
                 "kernel_config": {"n_tile": args.n_tile, "group_blocks": args.group_blocks,
                                   "schedule": args.schedule, "band_rows": args.band_rows,
@@ -436,6 +447,7 @@ def run_e2e(args, spec, a, b, out, cfg, dev, stream, linear, world, dist):
     from kairo_b200.ops import block_sparse_mm_bsr, sparse_linear
     from kairo_b200.types import BlockSparseMatrix
 
+    b = b.contiguous()  # this rank's columns of B (rows of X) as one host buffer
     h_blocks = a.blocks.to("cpu").pin_memory()
     h_rp = a.row_ptr.to("cpu").pin_memory()
     h_ci = a.col_idx.to("cpu").pin_memory()
@@ -891,6 +903,8 @@ def main() -> None:
     ap.add_argument("--schedule", choices=("auto", "rows", "bands"), default="auto")
     ap.add_argument("--band-rows", type=int, default=0)
     ap.add_argument("--gather", action="store_true", help="also time the all-gather of C (reported separately)")
+    ap.add_argument("--row-shards-only", action="store_true",
+                    help="at N > 1 split block-rows only (no column slices of B and C)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true")

@@ -7,6 +7,15 @@ rows of C with the single-GPU kernel, so the compute path has no collective.
 Only when the caller wants the whole C on every rank is an all-gather run
 (``gather_rows``: NCCL over NVLink for CUDA tensors, gloo for CPU tensors).
 
+With ``grid_shape`` the ranks form a (row groups x column slices) grid
+instead: each rank takes the block-rows of its row group and the columns of
+its slice of B and C.  Every rank must still read, once per sweep of its
+columns, the B panels its blocks touch, which on a uniform mask is all of
+them; a column slice cuts that compulsory B traffic by the number of slices
+(537 MB -> 134 MB per rank for the 262144^2 case at 8 GPUs, 2 x 4 grid) at
+the price of more row sweeps' worth of A per rank.  The work stays
+independent per rank.
+
 The reference has no multi-GPU code; this module is the sharding layer of the
 SpMM path (shard, compute, optional gather).
 """
@@ -83,6 +92,34 @@ def shard_bsr(a: BlockSparseMatrix, rank: int, world_size: int,
     return shard, RowShard(rank, world_size, r0, r1, n0, n1, bm)
 
 
+def grid_shape(world_size: int, n: int, min_cols: int = 256) -> tuple[int, int]:
+    """(row groups, column slices) for ``world_size`` ranks and N columns of
+    C: the most column slices (a power of two dividing world_size) that still
+    leave every rank at least ``min_cols`` columns; the rows are split among
+    the rest.  N = 1024 gives 1 x 2, 1 x 4 and 2 x 4 at 2, 4 and 8 ranks."""
+    if world_size <= 0:
+        raise ValueError("world_size must be positive")
+    pc = 1
+    while world_size % (2 * pc) == 0 and n // (2 * pc) >= min_cols:
+        pc *= 2
+    return world_size // pc, pc
+
+
+def column_range(n: int, parts: int, index: int, align: int = 128) -> tuple[int, int]:
+    """Columns [c0, c1) of slice ``index`` of ``parts``, cut at multiples of
+    ``align`` (whole kernel column tiles, 16-byte aligned B rows)."""
+    if not 0 <= index < parts:
+        raise ValueError("index outside [0, parts)")
+    units = (n + align - 1) // align
+    return min(n, (index * units // parts) * align), min(n, ((index + 1) * units // parts) * align)
+
+
+def grid_coords(rank: int, world_size: int, n: int, min_cols: int = 256) -> tuple[int, int, int, int]:
+    """(row group, column slice, row groups, column slices) of ``rank``."""
+    pr, pc = grid_shape(world_size, n, min_cols)
+    return rank // pc, rank % pc, pr, pc
+
+
 def gather_rows(c_local: torch.Tensor, bounds: list[int], block_rows: int, total_rows: int,
                 group=None) -> torch.Tensor:
     """All-gather row shards of C (unequal sizes) into the full (total_rows, N)
@@ -105,21 +142,59 @@ def gather_rows(c_local: torch.Tensor, bounds: list[int], block_rows: int, total
     return torch.cat(parts, dim=0)
 
 
+def gather_grid(c_local: torch.Tensor, bounds: list[int], block_rows: int, total_rows: int, n: int,
+                row_groups: int, col_slices: int, group=None) -> torch.Tensor:
+    """All-gather the (row group x column slice) tiles of C into the full
+    (total_rows, n) matrix on every rank (rank = row group * col_slices +
+    slice).  Tiles are padded to the largest one for one all-gather."""
+    world = dist.get_world_size(group)
+    rows = [max(0, min(total_rows, bounds[g + 1] * block_rows) - bounds[g] * block_rows) for g in range(row_groups)]
+    cols = [column_range(n, col_slices, j) for j in range(col_slices)]
+    pr_max = max(rows) if rows else 0
+    pc_max = max(c1 - c0 for c0, c1 in cols) if cols else 0
+    buf = torch.zeros(pr_max, pc_max, dtype=c_local.dtype, device=c_local.device)
+    buf[: c_local.shape[0], : c_local.shape[1]] = c_local
+    if c_local.is_cuda:
+        out = torch.empty(world * pr_max, pc_max, dtype=c_local.dtype, device=c_local.device)
+        dist.all_gather_into_tensor(out, buf, group=group)
+        tiles = [out[r * pr_max:(r + 1) * pr_max] for r in range(world)]
+    else:
+        tiles = [torch.empty_like(buf) for _ in range(world)]
+        dist.all_gather(tiles, buf, group=group)
+    full = torch.empty(total_rows, n, dtype=c_local.dtype, device=c_local.device)
+    for r in range(world):
+        g, j = divmod(r, col_slices)
+        r0 = bounds[g] * block_rows
+        c0, c1 = cols[j]
+        full[r0:r0 + rows[g], c0:c1] = tiles[r][: rows[g], : c1 - c0]
+    return full
+
+
 class ShardedSpmm:
     """C = A @ B with A sharded by block-rows over the ranks of ``group``.
 
     ``compute`` runs one rank's SpMM (default: the CUDA kernel through
     ``block_sparse_mm_bsr``); ``forward(B)`` returns this rank's rows of C, or
-    the full C on every rank with ``gather=True``.
+    the full C on every rank with ``gather=True``.  With ``n`` given (the
+    columns of B and C) the ranks form the ``grid_shape`` grid: each takes its
+    row group's block-rows and its column slice, ``forward`` returns that
+    tile of C, and ``gather=True`` assembles the whole C.
     """
 
     def __init__(self, a: BlockSparseMatrix, group=None,
-                 compute: Callable[[BlockSparseMatrix, torch.Tensor], torch.Tensor] | None = None) -> None:
+                 compute: Callable[[BlockSparseMatrix, torch.Tensor], torch.Tensor] | None = None,
+                 n: int | None = None) -> None:
         self.group = group
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
-        self.bounds = partition_rows(a.row_ptr, self.world)
-        self.local, self.shard = shard_bsr(a, self.rank, self.world, self.bounds)
+        self.n = n
+        if n is None:
+            self.row_groups, self.col_slices, self.row_group, self.col_slice = self.world, 1, self.rank, 0
+        else:
+            self.row_group, self.col_slice, self.row_groups, self.col_slices = grid_coords(self.rank, self.world, n)
+        self.bounds = partition_rows(a.row_ptr, self.row_groups)
+        self.local, self.shard = shard_bsr(a, self.row_group, self.row_groups, self.bounds)
+        self.columns = column_range(n, self.col_slices, self.col_slice) if n is not None else None
         self.total_rows = a.shape[0]
         if compute is None:
             from kairo_b200.ops.spmm import block_sparse_mm_bsr
@@ -128,6 +203,15 @@ class ShardedSpmm:
         self._compute = compute
 
     def forward(self, B: torch.Tensor, gather: bool = False) -> torch.Tensor:
+        if self.columns is not None:
+            if B.shape[1] != self.n:
+                raise ValueError(f"B must have {self.n} columns")
+            c0, c1 = self.columns
+            c_local = self._compute(self.local, B[:, c0:c1])
+            if not gather or self.world == 1:
+                return c_local
+            return gather_grid(c_local, self.bounds, self.shard.block_rows, self.total_rows, self.n,
+                               self.row_groups, self.col_slices, self.group)
         c_local = self._compute(self.local, B)
         if not gather or self.world == 1:
             return c_local

@@ -43,11 +43,50 @@ def _oracle_compute(K, N):
     from oracle import oracle
 
     def compute(a, B):
-        out = oracle.spmm_bsr_rows(a.row_ptr, a.col_idx, a.blk_idx, a.blocks, B, a.shape[0], K, N,
-                                   list(range(a.nbr)), nthreads=1)
+        out = oracle.spmm_bsr_rows(a.row_ptr, a.col_idx, a.blk_idx, a.blocks, B, a.shape[0], K,
+                                   B.shape[1] if N is None else N, list(range(a.nbr)), nthreads=1)
         return out[: a.shape[0]]
 
     return compute
+
+
+def _grid_problem(n=512):
+    """A seeded 48 x 40 block grid (bs 16) in BSR order and a B with n
+    columns, the same on every rank."""
+    from kairo_b200.types import BlockSparseMatrix
+
+    g = torch.Generator().manual_seed(17)
+    nbr, nbc, bs = 48, 40, 16
+    keep = torch.rand(nbr, nbc, generator=g) < 0.2
+    keep[5] = False  # an empty block-row
+    rows, cols = keep.nonzero(as_tuple=True)
+    counts = torch.bincount(rows, minlength=nbr)
+    row_ptr = torch.zeros(nbr + 1, dtype=torch.int32)
+    row_ptr[1:] = torch.cumsum(counts, 0).to(torch.int32)
+    blocks = torch.randn(rows.numel(), bs, bs, generator=g)
+    B = torch.randn(nbc * bs, n, generator=g)
+    a = BlockSparseMatrix(row_ptr=row_ptr, col_idx=cols.to(torch.int32), blocks=blocks, shape=(nbr * bs, nbc * bs),
+                          block_size=(bs, bs))
+    return a, B
+
+
+def _grid_worker(rank, world, port, out_dir):
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
+    try:
+        from kairo_b200.sharding import ShardedSpmm
+
+        a, B = _grid_problem()
+        s = ShardedSpmm(a, compute=_oracle_compute(a.shape[1], None), n=B.shape[1])
+        tile = s.forward(B, gather=False)
+        full = s.forward(B, gather=True)
+        torch.save({"tile": tile, "full": full, "grid": (s.row_groups, s.col_slices), "columns": s.columns,
+                    "rows": s.shard.rows}, Path(out_dir) / f"g{rank}.pt")
+    finally:
+        dist.destroy_process_group()
 
 
 def _worker(rank, world, port, case, out_dir, mode):
@@ -125,3 +164,49 @@ def test_rank_failure_surfaces_as_error_not_hang(tmp_path):
     msg = (tmp_path / "r0.err").read_text()
     seconds = float(msg.rsplit("after ", 1)[1].rstrip("s"))
     assert seconds < 60                    # ...within the process-group timeout
+
+
+def test_grid_shape_and_columns():
+    from kairo_b200.sharding import column_range, grid_coords, grid_shape
+
+    assert [grid_shape(w, 1024) for w in (1, 2, 4, 8)] == [(1, 1), (1, 2), (1, 4), (2, 4)]
+    assert grid_shape(8, 256) == (8, 1) and grid_shape(8, 8192) == (1, 8) and grid_shape(6, 4096) == (3, 2)
+    for n, parts in ((1024, 4), (1000, 3), (300, 2), (128, 1)):
+        cols = [column_range(n, parts, j) for j in range(parts)]
+        assert cols[0][0] == 0 and cols[-1][1] == n
+        assert all(cols[j][1] == cols[j + 1][0] for j in range(parts - 1))
+        assert all(c0 % 128 == 0 for c0, _ in cols)
+    assert grid_coords(5, 8, 1024) == (1, 1, 2, 4)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_grid_sharded_spmm_matches_single_process(world, tmp_path):
+    """(row groups x column slices) shards, computed with the oracle and
+    gathered, equal the single-process product bit for bit."""
+    from oracle import oracle
+
+    oracle.build()
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_grid_worker, args=(r, world, port, str(tmp_path))) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a rank did not finish")
+    a, B = _grid_problem()
+    full = oracle.spmm_bsr_rows(a.row_ptr, a.col_idx, None, a.blocks, B, a.shape[0], a.shape[1], B.shape[1],
+                                list(range(a.nbr)), nthreads=1)[: a.shape[0]]
+    covered = torch.zeros_like(full, dtype=torch.int32)
+    for r in range(world):
+        d = torch.load(tmp_path / f"g{r}.pt", weights_only=False)
+        assert d["grid"] == ((1, 2) if world == 2 else (2, 2))
+        assert torch.equal(d["full"], full)
+        (r0, r1), (c0, c1) = d["rows"], d["columns"]
+        r1 = min(r1, full.shape[0])
+        assert torch.equal(d["tile"], full[r0:r1, c0:c1])
+        covered[r0:r1, c0:c1] += 1
+    assert bool((covered == 1).all())
