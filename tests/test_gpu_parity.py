@@ -238,6 +238,23 @@ def test_acc_spmm_forward_fp32_reference_case():
     assert torch.allclose(cpu, out.cpu(), atol=1e-3)
 
 
+@pytest.mark.parametrize("case", [(torch.bfloat16, 32, 1024, 2048, 1024, 0.95, (256, 512)),
+                                  (torch.float16, 16, 512, 1024, 384, 0.9, (128, 384)),
+                                  (torch.float32, 16, 256, 512, 512, 0.8, (256, 512))])
+def test_spmm_on_a_column_slice_of_b(case):
+    """A rank of the multi-GPU grid multiplies by a column slice of the full
+    B: a strided view (leading dimension N, base offset c0) into a C tile."""
+    dtype, bs, m, k, n, sp, (c0, c1) = case
+    p = generate(WorkloadSpec("t", dtype, m, k, n, bs, sp), seed=13)
+    tiles, rows, cols, b = _to_dev(p)
+    a = bsr_from_tiles(tiles, rows, cols, (m, k))
+    view = b[:, c0:c1]
+    assert view.stride(0) == n and not view.is_contiguous()
+    c = block_sparse_mm_bsr(a, view, check=True)
+    ref = oracle.spmm_tiles(p.tiles, p.row_ids, p.col_ids, p.b[:, c0:c1].contiguous(), m, k, c1 - c0, bs)
+    assert rel_fro(c, ref) <= TOL
+
+
 def test_block_sparse_mm_out_dtype():
     """out_dtype=None / float32 give the fp32 product; A's dtype rounds it once."""
     M, K, N, tile = 128, 96, 64, 32
