@@ -60,6 +60,29 @@ def test_topk_indices_ties_and_nan():
     assert topk_indices(torch.tensor([-0.0, 0.0, -1.0]).to(DEV), 2).cpu().tolist() == [0, 1]
 
 
+def _ref_topk_ties(s: torch.Tensor, count: int) -> torch.Tensor:
+    """Indices of the `count` largest scores, ties to the lower index, NaN
+    lowest, -0.0 below +0.0 (the kernels' order-preserving key), ascending."""
+    import numpy as np
+
+    b = s.numpy().view(np.uint32)
+    key = np.where(b & 0x80000000, ~b, b | 0x80000000).astype(np.uint64)
+    key[np.isnan(s.numpy())] = 0
+    order = np.lexsort((np.arange(len(b)), -key.astype(np.int64)))
+    return torch.from_numpy(np.sort(order[:count]).astype(np.int64))
+
+
+@pytest.mark.parametrize("n", [5000, 1 << 18, 300000])
+def test_topk_indices_ties_quantised(n):
+    """Quantised scores (many ties at every threshold) and NaNs."""
+    g = torch.Generator().manual_seed(n)
+    s = torch.randint(-20, 20, (n,), generator=g).float() / 4
+    s[torch.randint(0, n, (n // 100,), generator=g)] = float("nan")
+    for count in (1, n // 7, n // 2, n - 3):
+        got = topk_indices(s.to(DEV), count).cpu()
+        assert torch.equal(got, _ref_topk_ties(s, count))
+
+
 def test_block_magnitude_mask_matches_reference_rule():
     g = torch.Generator().manual_seed(7)
     w = (torch.randn(1024, 4096, generator=g) * 0.02).to(torch.bfloat16)
