@@ -283,7 +283,7 @@ def run_ours(args) -> None:
     linear = spec.layout == "linear"
     b = problem.b[c0:c1] if linear else problem.b[:, c0:c1]
     cfg = KernelConfig(n_tile=args.n_tile, group_blocks=args.group_blocks, schedule=args.schedule,
-                       band_rows=args.band_rows)
+                       band_rows=args.band_rows, row_cost=args.row_cost)
     plan = describe(a, ncols, linear=linear, config=cfg)
     if linear:
         from kairo_b200.ops import sparse_linear
@@ -402,7 +402,7 @@ def run_ours(args) -> None:
                 "parallelism": (f"grid {row_groups}x{col_slices} (nnz-balanced block-row groups x column slices "
                                 f"of B and C, B replicated)"),
                 "l2": "flushed before every step (256 MiB write, untimed)",
-                "kernel_config": {"n_tile": args.n_tile, "group_blocks": args.group_blocks,
+                "kernel_config": {"n_tile": args.n_tile, "group_blocks": args.group_blocks, "row_cost": args.row_cost,
                                   "schedule": args.schedule, "band_rows": args.band_rows,
                                   "max_row_blocks": a.max_row_blocks},
                 "plan": plan,
@@ -902,6 +902,7 @@ def main() -> None:
     ap.add_argument("--group-blocks", type=int, default=0)
     ap.add_argument("--schedule", choices=("auto", "rows", "bands"), default="auto")
     ap.add_argument("--band-rows", type=int, default=0)
+    ap.add_argument("--row-cost", type=int, default=0, help="scheduler weight of a block-row (0 = library default)")
     ap.add_argument("--gather", action="store_true", help="also time the all-gather of C (reported separately)")
     ap.add_argument("--row-shards-only", action="store_true",
                     help="at N > 1 split block-rows only (no column slices of B and C)")
