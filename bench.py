@@ -256,11 +256,16 @@ def run_ours(args) -> None:
         raise SystemExit("bench.py needs a CUDA device")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    json_fd = None
     if world > 1:
         from datetime import timedelta
 
-        # NCCL's version banner goes to stdout, where the one JSON line of
-        # rank 0 must stand alone; keep warnings, unless more was asked for.
+        # The communicator set-up can write a version banner to stdout, where
+        # rank 0's one JSON line must stand alone: until that line, file
+        # descriptor 1 points at stderr, and the line goes to the saved one.
+        sys.stdout.flush()
+        json_fd = os.dup(1)
+        os.dup2(2, 1)
         if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
             os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
@@ -431,7 +436,11 @@ def run_ours(args) -> None:
         }
         if gather_ms is not None:
             line["gather_ms"] = gather_ms
-        print(json.dumps(line), flush=True)
+        if json_fd is not None:
+            sys.stdout.flush()
+            os.write(json_fd, (json.dumps(line) + "\n").encode())
+        else:
+            print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
