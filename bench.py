@@ -249,7 +249,7 @@ def run_ours(args) -> None:
     import torch.distributed as dist
 
     from kairo_b200.ops import KernelConfig, block_sparse_mm_bsr, bsr_from_tiles, describe
-    from kairo_b200.sharding import column_range, gather_grid, grid_coords, partition_rows, shard_bsr
+    from kairo_b200.sharding import column_range, gather_grid, grid_coords, operand_bytes, partition_rows, shard_bsr
 
     rank, world, local = dist_env()
     if not torch.cuda.is_available():
@@ -276,7 +276,8 @@ def run_ours(args) -> None:
     # Ranks form a (row groups x column slices) grid: block-rows balanced by
     # nonzero count within the row groups, C's columns (the batch rows of X
     # in the linear layout) sliced; no collective on the compute path.
-    row_group, col_slice, row_groups, col_slices = grid_coords(rank, world, spec.n)
+    row_group, col_slice, row_groups, col_slices = grid_coords(rank, world, spec.n, 256,
+                                                               *operand_bytes(a_full, spec.n))
     if args.row_shards_only:
         row_group, col_slice, row_groups, col_slices = rank, 0, world, 1
     bounds = partition_rows(a_full.row_ptr, row_groups)

@@ -12,9 +12,9 @@ instead: each rank takes the block-rows of its row group and the columns of
 its slice of B and C.  Every rank must still read, once per sweep of its
 columns, the B panels its blocks touch, which on a uniform mask is all of
 them; a column slice cuts that compulsory B traffic by the number of slices
-(537 MB -> 134 MB per rank for the 262144^2 case at 8 GPUs, 2 x 4 grid) at
-the price of more row sweeps' worth of A per rank.  The work stays
-independent per rank.
+(537 MB -> 268 MB per rank for the 262144^2 case at 8 GPUs, 4 x 2 grid) at
+the price of a larger share of A per rank; ``grid_shape`` balances the two.
+The work stays independent per rank.
 
 The reference has no multi-GPU code; this module is the sharding layer of the
 SpMM path (shard, compute, optional gather).
@@ -92,16 +92,26 @@ def shard_bsr(a: BlockSparseMatrix, rank: int, world_size: int,
     return shard, RowShard(rank, world_size, r0, r1, n0, n1, bm)
 
 
-def grid_shape(world_size: int, n: int, min_cols: int = 256) -> tuple[int, int]:
+def grid_shape(world_size: int, n: int, min_cols: int = 256, a_bytes: int | None = None,
+               b_bytes: int | None = None) -> tuple[int, int]:
     """(row groups, column slices) for ``world_size`` ranks and N columns of
-    C: the most column slices (a power of two dividing world_size) that still
-    leave every rank at least ``min_cols`` columns; the rows are split among
-    the rest.  N = 1024 gives 1 x 2, 1 x 4 and 2 x 4 at 2, 4 and 8 ranks."""
+    C.  Column slices are powers of two dividing world_size that leave every
+    rank at least ``min_cols`` columns.  Given the sizes of A (blocks and
+    indices) and B, the shape minimises the bytes one rank holds and reads
+    at least once, A / row_groups + B / column_slices (what its compulsory
+    DRAM reads and its host uploads scale with); without them it takes the
+    most column slices.  For the 262144^2 case (A 687 MB, B 537 MB, N 1024)
+    that is 2 x 1, 2 x 2 and 4 x 2 at 2, 4 and 8 ranks."""
     if world_size <= 0:
         raise ValueError("world_size must be positive")
-    pc = 1
-    while world_size % (2 * pc) == 0 and n // (2 * pc) >= min_cols:
-        pc *= 2
+    options = [1]
+    while world_size % (2 * options[-1]) == 0 and n // (2 * options[-1]) >= min_cols:
+        options.append(2 * options[-1])
+    if a_bytes is None or b_bytes is None:
+        pc = options[-1]
+    else:
+        # ties go to fewer column slices (the plain row split)
+        pc = min(options, key=lambda c: (a_bytes * c + b_bytes * (world_size // c), c))
     return world_size // pc, pc
 
 
@@ -114,10 +124,18 @@ def column_range(n: int, parts: int, index: int, align: int = 128) -> tuple[int,
     return min(n, (index * units // parts) * align), min(n, ((index + 1) * units // parts) * align)
 
 
-def grid_coords(rank: int, world_size: int, n: int, min_cols: int = 256) -> tuple[int, int, int, int]:
+def grid_coords(rank: int, world_size: int, n: int, min_cols: int = 256, a_bytes: int | None = None,
+                b_bytes: int | None = None) -> tuple[int, int, int, int]:
     """(row group, column slice, row groups, column slices) of ``rank``."""
-    pr, pc = grid_shape(world_size, n, min_cols)
+    pr, pc = grid_shape(world_size, n, min_cols, a_bytes, b_bytes)
     return rank // pc, rank % pc, pr, pc
+
+
+def operand_bytes(a: BlockSparseMatrix, n: int) -> tuple[int, int]:
+    """(bytes of A's blocks and indices, bytes of a (K x n) B in A's dtype)."""
+    bm, bk = a.block_size
+    es = a.blocks.element_size()
+    return a.nnzb * (bm * bk * es + 4) + (a.nbr + 1) * 4, a.shape[1] * n * es
 
 
 def gather_rows(c_local: torch.Tensor, bounds: list[int], block_rows: int, total_rows: int,
@@ -191,7 +209,8 @@ class ShardedSpmm:
         if n is None:
             self.row_groups, self.col_slices, self.row_group, self.col_slice = self.world, 1, self.rank, 0
         else:
-            self.row_group, self.col_slice, self.row_groups, self.col_slices = grid_coords(self.rank, self.world, n)
+            self.row_group, self.col_slice, self.row_groups, self.col_slices = grid_coords(
+                self.rank, self.world, n, 256, *operand_bytes(a, n))
         self.bounds = partition_rows(a.row_ptr, self.row_groups)
         self.local, self.shard = shard_bsr(a, self.row_group, self.row_groups, self.bounds)
         self.columns = column_range(n, self.col_slices, self.col_slice) if n is not None else None

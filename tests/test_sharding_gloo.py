@@ -177,6 +177,11 @@ def test_grid_shape_and_columns():
         assert all(cols[j][1] == cols[j + 1][0] for j in range(parts - 1))
         assert all(c0 % 128 == 0 for c0, _ in cols)
     assert grid_coords(5, 8, 1024) == (1, 1, 2, 4)
+    # sized: A / row groups + B / column slices per rank, smallest wins
+    a_b, b_b = 687_000_000, 537_000_000
+    assert [grid_shape(w, 1024, a_bytes=a_b, b_bytes=b_b) for w in (1, 2, 4, 8)] == [(1, 1), (2, 1), (2, 2), (4, 2)]
+    assert grid_shape(8, 1024, a_bytes=10, b_bytes=10_000) == (2, 4)        # B dominates: most slices allowed
+    assert grid_shape(8, 1024, a_bytes=10_000, b_bytes=10) == (8, 1)        # A dominates: rows only
 
 
 @pytest.mark.parametrize("world", [2, 4])
