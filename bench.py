@@ -273,13 +273,14 @@ def run_ours(args) -> None:
     t0 = time.perf_counter()
     problem = generate(spec, seed=args.seed, device=dev)
     a_full = bsr_from_tiles(problem.tiles, problem.row_ids, problem.col_ids, (spec.m, spec.k))
-    # Ranks form a (row groups x column slices) grid: block-rows balanced by
-    # nonzero count within the row groups, C's columns (the batch rows of X
-    # in the linear layout) sliced; no collective on the compute path.
-    row_group, col_slice, row_groups, col_slices = grid_coords(rank, world, spec.n, 256,
-                                                               *operand_bytes(a_full, spec.n))
-    if args.row_shards_only:
-        row_group, col_slice, row_groups, col_slices = rank, 0, world, 1
+    # Default: the configuration's decomposition, nnz-balanced block-row
+    # ranges with B replicated.  --grid: ranks form a (row groups x column
+    # slices) grid, C's columns (the batch rows of X in the linear layout)
+    # sliced as well.  No collective on the compute path either way.
+    row_group, col_slice, row_groups, col_slices = rank, 0, world, 1
+    if args.grid:
+        row_group, col_slice, row_groups, col_slices = grid_coords(rank, world, spec.n, 256,
+                                                                   *operand_bytes(a_full, spec.n))
     bounds = partition_rows(a_full.row_ptr, row_groups)
     a, shard = shard_bsr(a_full, row_group, row_groups, bounds)
     c0, c1 = column_range(spec.n, col_slices, col_slice)
@@ -914,8 +915,9 @@ def main() -> None:
     ap.add_argument("--band-rows", type=int, default=0)
     ap.add_argument("--row-cost", type=int, default=0, help="scheduler weight of a block-row (0 = library default)")
     ap.add_argument("--gather", action="store_true", help="also time the all-gather of C (reported separately)")
-    ap.add_argument("--row-shards-only", action="store_true",
-                    help="at N > 1 split block-rows only (no column slices of B and C)")
+    ap.add_argument("--grid", action="store_true",
+                    help="at N > 1 arrange the ranks as block-row groups x column slices of B and C "
+                         "(default: block-row ranges only, B replicated)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true")

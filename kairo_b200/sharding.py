@@ -7,8 +7,8 @@ rows of C with the single-GPU kernel, so the compute path has no collective.
 Only when the caller wants the whole C on every rank is an all-gather run
 (``gather_rows``: NCCL over NVLink for CUDA tensors, gloo for CPU tensors).
 
-With ``grid_shape`` the ranks form a (row groups x column slices) grid
-instead: each rank takes the block-rows of its row group and the columns of
+Optionally (``ShardedSpmm(a, n=N)``) the ranks form a (row groups x column
+slices) grid instead, chosen by ``grid_shape``: each rank takes the block-rows of its row group and the columns of
 its slice of B and C.  Every rank must still read, once per sweep of its
 columns, the B panels its blocks touch, which on a uniform mask is all of
 them; a column slice cuts that compulsory B traffic by the number of slices
