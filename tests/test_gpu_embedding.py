@@ -172,6 +172,19 @@ def test_scatter_vs_oracle(dtype, case):
     assert torch.equal(_bits(got), _bits(exp.to(dtype)))
 
 
+def test_scatter_mostly_inactive_batch():
+    # Nearly every batch position names an inactive row: they all share the
+    # bucket after the active ones, one longer than the shared-memory sort
+    # takes, which the sums must ignore.
+    gen = torch.Generator().manual_seed(12)
+    n, d, b = 100000, 32, 50000
+    batch = torch.randint(0, n, (b,), generator=gen)
+    active = torch.unique(batch[:3])
+    grad = torch.randn(b, d, generator=gen)
+    got = sparse_scatter_grad(grad.to(DEV), active.to(DEV), batch.to(DEV), n, d, check=True)
+    assert torch.equal(got.cpu(), oracle.sparse_scatter_grad(grad, active, batch, n, d))
+
+
 def test_scatter_edge_cases():
     g = torch.randn(3, 4, device=DEV)
     e = torch.tensor([], dtype=torch.int64, device=DEV)

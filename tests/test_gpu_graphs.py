@@ -97,3 +97,31 @@ def test_sparse_gather_graph_replay():
     torch.cuda.synchronize()
     _, rs, cs = oracle.sort_coo_by_row(idx[0], idx[1], n)
     assert torch.equal(holder["out"].cpu(), oracle.sparse_gather(w.cpu(), oracle.row_offsets(rs, n), cs, ids2))
+
+
+def test_sparse_scatter_grad_graph_replay():
+    # A replay with new batch ids and gradients must clear and rewrite every
+    # row (the clearing, key search, bucket sort and sums are all captured).
+    from kairo_b200.ops import sparse_scatter_grad
+
+    gen = torch.Generator().manual_seed(8)
+    n, d, b = 5000, 64, 3000
+    batch = torch.randint(0, n, (b,), generator=gen)
+    active = torch.unique(batch)[::2].contiguous()
+    grad = torch.randn(b, d, generator=gen).to(DEV)
+    bid = batch.to(DEV)
+    aid = active.to(DEV)
+    holder = {}
+
+    def step():
+        holder["out"] = sparse_scatter_grad(grad, aid, bid, n, d)
+
+    g = _capture(step)
+    batch2 = torch.randint(0, n, (b,), generator=gen)
+    grad2 = torch.randn(b, d, generator=gen)
+    bid.copy_(batch2.to(DEV))
+    grad.copy_(grad2.to(DEV))
+    holder["out"].fill_(float("nan"))
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(holder["out"].cpu(), oracle.sparse_scatter_grad(grad2, active, batch2, n, d))
