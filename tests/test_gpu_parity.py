@@ -155,7 +155,8 @@ def test_tcgen05_spmm_vs_oracle(case):
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
-@pytest.mark.parametrize("shape", [(256, 256, 64, 16), (4096, 4096, 256, 16), (130, 90, 33, 32), (256, 256, 128, 64)])
+@pytest.mark.parametrize("shape", [(256, 256, 64, 16), (4096, 4096, 256, 16), (512, 512, 200, 16), (130, 90, 33, 32),
+                                   (256, 256, 128, 64)])
 def test_simt_spmm_vs_oracle(dtype, shape):
     m, k, n, bs = shape
     spec = WorkloadSpec("t", dtype, m, k, n, bs, 0.9 if m > 1000 else 0.6)
