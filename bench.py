@@ -289,8 +289,8 @@ def run_ours(args) -> None:
     local_rows = a.shape[0]
     linear = spec.layout == "linear"
     b = problem.b[c0:c1] if linear else problem.b[:, c0:c1]
-    cfg = KernelConfig(n_tile=args.n_tile, group_blocks=args.group_blocks, schedule=args.schedule,
-                       band_rows=args.band_rows, row_cost=args.row_cost)
+    cfg = KernelConfig(kernel=args.kernel, n_tile=args.n_tile, group_blocks=args.group_blocks,
+                       schedule=args.schedule, band_rows=args.band_rows, row_cost=args.row_cost)
     plan = describe(a, ncols, linear=linear, config=cfg)
     if linear:
         from kairo_b200.ops import sparse_linear
@@ -409,7 +409,8 @@ def run_ours(args) -> None:
                 "parallelism": (f"grid {row_groups}x{col_slices} (nnz-balanced block-row groups x column slices "
                                 f"of B and C, B replicated)"),
                 "l2": "flushed before every step (256 MiB write, untimed)",
-                "kernel_config": {"n_tile": args.n_tile, "group_blocks": args.group_blocks, "row_cost": args.row_cost,
+                "kernel_config": {"kernel": args.kernel, "n_tile": args.n_tile, "group_blocks": args.group_blocks,
+                                  "row_cost": args.row_cost,
                                   "schedule": args.schedule, "band_rows": args.band_rows,
                                   "max_row_blocks": a.max_row_blocks},
                 "plan": plan,
@@ -909,6 +910,8 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--shape", default="", help="MxKxN override of the workload's sizes (same density), "
                     "for profiling smaller cases")
+    ap.add_argument("--kernel", choices=("auto", "simt", "tcgen05", "split_bf16"), default="auto",
+                    help="kernel family (split_bf16: fp32 workloads on the tensor cores, opt-in)")
     ap.add_argument("--n-tile", type=int, default=0)
     ap.add_argument("--group-blocks", type=int, default=0)
     ap.add_argument("--schedule", choices=("auto", "rows", "bands"), default="auto")

@@ -67,7 +67,11 @@ typedef enum kairo_dtype {
 typedef enum kairo_kernel {
   KAIRO_KERNEL_AUTO = 0,     /* tcgen05 for f16/bf16 when the shape allows it, else SIMT */
   KAIRO_KERNEL_SIMT = 1,     /* CUDA-core FMA kernel (fp32 path, any shape) */
-  KAIRO_KERNEL_TCGEN05 = 2   /* TMA + tcgen05/TMEM persistent kernel (f16/bf16) */
+  KAIRO_KERNEL_TCGEN05 = 2,  /* TMA + tcgen05/TMEM persistent kernel (f16/bf16) */
+  KAIRO_KERNEL_SPLIT_BF16 = 3  /* opt-in, fp32 A and B: the tcgen05 kernel on a bf16 hi/lo split,
+                                  A_hi B_hi + A_hi B_lo + A_lo B_hi (about 2^-15 relative error per
+                                  product); square 16/32/64 blocks, STANDARD layout.  Needs extra
+                                  workspace for the derived operands.  No reference counterpart. */
 } kairo_kernel;
 
 /* Device error codes written to the workspace error word (low 8 bits). */

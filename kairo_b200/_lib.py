@@ -36,6 +36,7 @@ DTYPE_BF16 = 2
 KERNEL_AUTO = 0
 KERNEL_SIMT = 1
 KERNEL_TCGEN05 = 2
+KERNEL_SPLIT_BF16 = 3
 
 LAYOUT_STANDARD = 0
 LAYOUT_LINEAR = 1

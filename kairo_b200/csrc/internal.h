@@ -123,6 +123,19 @@ kairo_status tc_launch(const kairo_bsr* a, const void* b, int64_t ldb, int32_t l
                        void* c, int64_t ldc, kairo_dtype c_dtype, const TcPlan& plan,
                        void* workspace, cudaStream_t stream);
 
+// fp32 on the tcgen05 kernel by a bf16 hi/lo split (spmm_split.cu).  The
+// derived operands occupy `bytes` of workspace: blocks (3 nnzb, bm, bk)
+// bf16, block-column indices, row pointers, and a (k, ldb) bf16 B.
+struct SplitLayout {
+  int64_t ldb;  // leading dimension of the derived B (N rounded up to 8)
+  int64_t k;    // rows of the derived B: 3 * nbc * bk
+  size_t blocks_off, col_idx_off, row_ptr_off, b_off, bytes;
+};
+SplitLayout split_bf16_layout(const kairo_bsr* a, int64_t n);
+kairo_bsr split_bf16_desc(const kairo_bsr* a, const SplitLayout& l, void* base);
+kairo_status split_bf16_prepare(const kairo_bsr* a, const void* b, int64_t ldb, int64_t n, const SplitLayout& l,
+                                void* base, cudaStream_t s);
+
 // SIMT path (spmm_simt.cu)
 bool simt_supported(const kairo_bsr* a, int32_t layout, kairo_dtype c_dtype, std::string* why);
 kairo_status simt_launch(const kairo_bsr* a, const void* b, int64_t ldb, int64_t n, void* c,

@@ -81,13 +81,17 @@ kairo_status validate_bsr(const kairo_bsr* a) {
   return KAIRO_STATUS_SUCCESS;
 }
 
-enum class Path { kNone, kZero, kSimt, kTc, kBand };
+enum class Path { kNone, kZero, kSimt, kTc, kBand, kSplit };
 
 struct Choice {
   Path path = Path::kNone;
   TcPlan plan{};
   BandPlan band{};
+  SplitLayout split{};  // kSplit: derived operands after the tcgen05 workspace
+  size_t split_base = 0;
 };
+
+size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 kairo_status choose(const kairo_bsr* a, const void* b, int64_t ldb, int32_t layout, int64_t n, const void* c,
                     int64_t ldc, kairo_dtype c_dtype, const kairo_spmm_config* cfg, Choice* out) {
@@ -121,9 +125,28 @@ kairo_status choose(const kairo_bsr* a, const void* b, int64_t ldb, int32_t layo
   const int schedule = cfg ? cfg->schedule : KAIRO_SCHEDULE_AUTO;
   if (schedule != KAIRO_SCHEDULE_AUTO && schedule != KAIRO_SCHEDULE_ROWS && schedule != KAIRO_SCHEDULE_BANDS)
     return fail(KAIRO_STATUS_INVALID_VALUE, "unknown schedule selector");
-  if (schedule == KAIRO_SCHEDULE_BANDS && kernel == KAIRO_KERNEL_SIMT)
+  if (schedule == KAIRO_SCHEDULE_BANDS && (kernel == KAIRO_KERNEL_SIMT || kernel == KAIRO_KERNEL_SPLIT_BF16))
     return fail(KAIRO_STATUS_INVALID_VALUE, "the band schedule runs on the tcgen05 kernel only");
-  if (kernel == KAIRO_KERNEL_TCGEN05 || (kernel == KAIRO_KERNEL_AUTO && tc_ok)) {
+  if (kernel == KAIRO_KERNEL_SPLIT_BF16) {
+    if (a->dtype != KAIRO_DTYPE_F32) return fail(KAIRO_STATUS_NOT_SUPPORTED, "the split-bf16 kernel takes fp32 input");
+    if (layout != KAIRO_LAYOUT_STANDARD)
+      return fail(KAIRO_STATUS_NOT_SUPPORTED, "the split-bf16 kernel implements the STANDARD layout only");
+    if (3 * a->nnzb > INT32_MAX) return fail(KAIRO_STATUS_NOT_SUPPORTED, "too many blocks for the split-bf16 kernel");
+    if (reinterpret_cast<uintptr_t>(a->blocks) & 15u)
+      return fail(KAIRO_STATUS_NOT_SUPPORTED, "the split-bf16 kernel needs 16-byte aligned block storage");
+    // Plan on the derived bf16 operands, with aligned stand-in pointers.
+    static const uint8_t dummy[16] __attribute__((aligned(16))) = {0};
+    ch.split = split_bf16_layout(a, n);
+    kairo_bsr d = split_bf16_desc(a, ch.split, const_cast<uint8_t*>(dummy));
+    d.blocks = dummy;
+    std::string why;
+    if (!tc_supported(&d, layout, n, ch.split.ldb, ldc, c_dtype, dummy, c, &why))
+      return fail(KAIRO_STATUS_NOT_SUPPORTED, why);
+    ch.path = Path::kSplit;
+    st = tc_plan(&d, layout, n, cfg, current_device(), &ch.plan);
+    if (st) return st;
+    ch.split_base = align256(ch.plan.workspace_bytes);
+  } else if (kernel == KAIRO_KERNEL_TCGEN05 || (kernel == KAIRO_KERNEL_AUTO && tc_ok)) {
     if (!tc_ok) return fail(KAIRO_STATUS_NOT_SUPPORTED, why_tc);
     const int dev = current_device();
     std::string why_band;
@@ -152,6 +175,7 @@ kairo_status choose(const kairo_bsr* a, const void* b, int64_t ldb, int32_t layo
 size_t ws_bytes_for(const Choice& ch) {
   if (ch.path == Path::kTc) return ch.plan.workspace_bytes;
   if (ch.path == Path::kBand) return ch.band.workspace_bytes;
+  if (ch.path == Path::kSplit) return ch.split_base + ch.split.bytes;
   return kWorkspaceHeaderBytes + kCounterRegionBytes;
 }
 
@@ -249,6 +273,16 @@ kairo_status kairo_bsr_spmm_describe(const kairo_bsr* a, int32_t layout, int64_t
       p.group_blocks = ch.plan.group;
       p.rows = ch.plan.row_cost;
       break;
+    case Path::kSplit:
+      p.kernel = KAIRO_KERNEL_SPLIT_BF16;
+      p.schedule = KAIRO_SCHEDULE_ROWS;
+      p.launches = 3;
+      p.grid = ch.plan.grid;
+      p.n_tile = 128 * ch.plan.nt;
+      p.stages = ch.plan.stages;
+      p.group_blocks = ch.plan.group;
+      p.rows = ch.plan.row_cost;
+      break;
     case Path::kBand:
       p.kernel = KAIRO_KERNEL_TCGEN05;
       p.schedule = KAIRO_SCHEDULE_BANDS;
@@ -287,6 +321,14 @@ kairo_status kairo_bsr_spmm(const kairo_bsr* a, const void* b, int64_t ldb, int3
   }
   if (ch.path == Path::kTc) return tc_launch(a, b, ldb, layout, n, c, ldc, c_dtype, ch.plan, workspace, s);
   if (ch.path == Path::kBand) return band_launch(a, b, ldb, layout, n, c, ldc, c_dtype, ch.band, workspace, s);
+  if (ch.path == Path::kSplit) {
+    void* base = static_cast<uint8_t*>(workspace) + ch.split_base;
+    st = split_bf16_prepare(a, b, ldb, n, ch.split, base, s);
+    if (st) return st;
+    const kairo_bsr d = split_bf16_desc(a, ch.split, base);
+    return tc_launch(&d, static_cast<uint8_t*>(base) + ch.split.b_off, ch.split.ldb, layout, n, c, ldc, c_dtype,
+                     ch.plan, workspace, s);
+  }
   return simt_launch(a, b, ldb, n, c, ldc, workspace, s);
 }
 

@@ -27,7 +27,9 @@ from kairo_b200.types import BlockSparseMatrix, SparseMask
 class KernelConfig:
     """Launch knobs of the BSR SpMM (0 = library default).
 
-    kernel: "auto", "simt" or "tcgen05"; n_tile: C columns per work item on
+    kernel: "auto", "simt", "tcgen05" or "split_bf16" (opt-in, fp32 input:
+    the tcgen05 kernel on a bf16 hi/lo split of A and B, hi·hi + hi·lo +
+    lo·hi, about 2^-15 relative error per product); n_tile: C columns per work item on
     the tcgen05 kernel (128 or 256); stages: pipeline stages in shared
     memory; row_cost: scheduler weight of a block-row in units of one block
     (row-split schedule); num_ctas: persistent grid size; group_blocks:
@@ -47,8 +49,8 @@ class KernelConfig:
     band_rows: int = 0
 
     def __post_init__(self) -> None:
-        if self.kernel not in ("auto", "simt", "tcgen05"):
-            raise ValueError(f"kernel must be 'auto', 'simt' or 'tcgen05', got {self.kernel!r}")
+        if self.kernel not in ("auto", "simt", "tcgen05", "split_bf16"):
+            raise ValueError(f"kernel must be 'auto', 'simt', 'tcgen05' or 'split_bf16', got {self.kernel!r}")
         if self.n_tile not in (0, 128, 256):
             raise ValueError(f"n_tile must be 0, 128 or 256, got {self.n_tile}")
         if self.schedule not in ("auto", "rows", "bands"):
@@ -61,7 +63,8 @@ class KernelConfig:
 
     def to_c(self) -> _lib.KairoSpmmConfig:
         c = _lib.KairoSpmmConfig()
-        c.kernel = {"auto": _lib.KERNEL_AUTO, "simt": _lib.KERNEL_SIMT, "tcgen05": _lib.KERNEL_TCGEN05}[self.kernel]
+        c.kernel = {"auto": _lib.KERNEL_AUTO, "simt": _lib.KERNEL_SIMT, "tcgen05": _lib.KERNEL_TCGEN05,
+                    "split_bf16": _lib.KERNEL_SPLIT_BF16}[self.kernel]
         c.n_tile = self.n_tile
         c.stages = self.stages
         c.row_cost = self.row_cost
@@ -229,7 +232,8 @@ def describe(a: BlockSparseMatrix, n: int, *, linear: bool = False, config: Kern
     with torch.cuda.device(a.device):
         _lib.check(lib.kairo_bsr_spmm_describe(ctypes.byref(desc), layout, int(n), ctypes.byref(cfg),
                                                ctypes.byref(plan)), "describe")
-    kernel = {0: "none", _lib.KERNEL_SIMT: "simt", _lib.KERNEL_TCGEN05: "tcgen05"}[plan.kernel]
+    kernel = {0: "none", _lib.KERNEL_SIMT: "simt", _lib.KERNEL_TCGEN05: "tcgen05",
+              _lib.KERNEL_SPLIT_BF16: "split_bf16"}[plan.kernel]
     schedule = {0: "none", _lib.SCHEDULE_ROWS: "rows", _lib.SCHEDULE_BANDS: "bands"}[plan.schedule]
     return {"kernel": kernel, "schedule": schedule, "launches": plan.launches, "grid": plan.grid,
             "n_tile": plan.n_tile, "stages": plan.stages, "group_blocks": plan.group_blocks, "rows": plan.rows,

@@ -320,3 +320,40 @@ def test_workspace_error_word_clean():
     block_sparse_mm_bsr(a, b)
     ws = _lib.workspace(0, torch.device(DEV))
     assert _lib.read_workspace_error(ws, clear=False) == 0
+
+
+# The opt-in split-bf16 kernel takes fp32 A and B through the tcgen05 kernel
+# as hi·hi + hi·lo + lo·hi of a bf16 hi/lo split; its error is about 1e-5
+# relative (the dropped lo·lo term), so it is held to a bar ten times tighter
+# than the 1e-3 parity bar.
+SPLIT_TOL = 1e-4
+
+
+@pytest.mark.parametrize("shape", [(4096, 4096, 256, 16), (512, 512, 200, 32), (256, 256, 128, 64),
+                                   (130, 90, 64, 16)])
+def test_split_bf16_spmm_vs_oracle(shape):
+    m, k, n, bs = shape
+    spec = WorkloadSpec("t", torch.float32, m, k, n, bs, 0.9 if m > 1000 else 0.6)
+    p = generate(spec, seed=3)
+    tiles, rows, cols, b = _to_dev(p)
+    a = bsr_from_tiles(tiles, rows, cols, (m, k))
+    cfg = KernelConfig(kernel="split_bf16")
+    from kairo_b200.ops import describe
+    assert describe(a, n, config=cfg)["kernel"] == "split_bf16"
+    c = block_sparse_mm_bsr(a, b, config=cfg, check=True)
+    err = rel_fro(c, _oracle_c(p))
+    assert err <= SPLIT_TOL, f"relative Frobenius error {err:.3e}"
+    assert torch.equal(c, block_sparse_mm_bsr(a, b, config=cfg, check=True))
+
+
+def test_split_bf16_spmm_unsupported():
+    g = torch.Generator().manual_seed(4)
+    tiles = torch.randn(3, 16, 8, generator=g)
+    a = bsr_from_tiles(tiles.to(DEV), torch.tensor([0, 1, 1]).to(DEV), torch.tensor([0, 0, 1]).to(DEV), (32, 16))
+    with pytest.raises(_lib.KairoError):
+        block_sparse_mm_bsr(a, torch.randn(16, 64, device=DEV), config=KernelConfig(kernel="split_bf16"))
+    sq = bsr_from_tiles(torch.randn(2, 16, 16, generator=g).to(torch.bfloat16).to(DEV),
+                        torch.tensor([0, 1]).to(DEV), torch.tensor([0, 0]).to(DEV), (32, 16))
+    with pytest.raises(_lib.KairoError):
+        block_sparse_mm_bsr(sq, torch.randn(16, 64, device=DEV).to(torch.bfloat16),
+                            config=KernelConfig(kernel="split_bf16"))
