@@ -92,22 +92,35 @@ __global__ void k_split_blocks(const float* __restrict__ blocks, const int32_t* 
 
 // Derived B: row (3c + t) * bk + kk holds B's row c * bk + kk as hi (t = 0,
 // 2) or lo (t = 1); rows past K are zero.  Threads run over the columns of
-// one source row (gridDim.y strides the rows), so no index is divided.
+// kRowsPerPass source rows at a time (gridDim.y strides the row groups), so
+// each thread has that many independent loads in flight and no per-element
+// index is divided.
+constexpr int kRowsPerPass = 4;
+
 __global__ void k_split_b(const float* __restrict__ b, int64_t ldb, int64_t k, int64_t n, int32_t bk, int64_t k_src,
                           int64_t ldb_out, __nv_bfloat16* __restrict__ out) {
-  for (int64_t r = blockIdx.y; r < k_src; r += gridDim.y) {
-    const int64_t c = r / bk;  // once per row and CTA
-    const int64_t kk = r - c * bk;
-    __nv_bfloat16* o_hi0 = out + ((3 * c + 0) * bk + kk) * ldb_out;
-    __nv_bfloat16* o_lo = out + ((3 * c + 1) * bk + kk) * ldb_out;
-    __nv_bfloat16* o_hi2 = out + ((3 * c + 2) * bk + kk) * ldb_out;
+  for (int64_t r0 = static_cast<int64_t>(blockIdx.y) * kRowsPerPass; r0 < k_src;
+       r0 += static_cast<int64_t>(gridDim.y) * kRowsPerPass) {
     for (int64_t col = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; col < n;
          col += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-      __nv_bfloat16 hi = __float2bfloat16_rn(0.f), lo = hi;
-      if (r < k) split_bf16(b[r * ldb + col], &hi, &lo);
-      o_hi0[col] = hi;
-      o_lo[col] = lo;
-      o_hi2[col] = hi;
+      float v[kRowsPerPass];
+#pragma unroll
+      for (int u = 0; u < kRowsPerPass; ++u) {
+        const int64_t r = r0 + u;
+        v[u] = (r < k) ? b[r * ldb + col] : 0.f;  // rows in [k, k_src) are the zero padding
+      }
+#pragma unroll
+      for (int u = 0; u < kRowsPerPass; ++u) {
+        const int64_t r = r0 + u;
+        if (r >= k_src) break;
+        const int64_t c = r / bk;
+        const int64_t kk = r - c * bk;
+        __nv_bfloat16 hi, lo;
+        split_bf16(v[u], &hi, &lo);
+        out[((3 * c + 0) * bk + kk) * ldb_out + col] = hi;
+        out[((3 * c + 1) * bk + kk) * ldb_out + col] = lo;
+        out[((3 * c + 2) * bk + kk) * ldb_out + col] = hi;
+      }
     }
   }
 }
@@ -159,7 +172,7 @@ kairo_status split_bf16_prepare(const kairo_bsr* a, const void* b, int64_t ldb, 
   if (e != cudaSuccess) return cuda_fail(e, "launch of the split-bf16 block kernel");
   const int64_t k_src = l.k / 3;  // nbc * bk source rows, the last slab zero-padded past K
   const dim3 gb(static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 64)),
-                static_cast<unsigned>(std::min<int64_t>(k_src, 65535)));
+                static_cast<unsigned>(std::min<int64_t>((k_src + kRowsPerPass - 1) / kRowsPerPass, 148 * 4)));
   k_split_b<<<gb, 256, 0, s>>>(static_cast<const float*>(b), ldb, a->cols, n, a->bk, k_src, l.ldb,
                                reinterpret_cast<__nv_bfloat16*>(p + l.b_off));
   e = cudaGetLastError();
