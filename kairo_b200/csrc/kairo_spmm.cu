@@ -276,7 +276,7 @@ kairo_status kairo_bsr_spmm_describe(const kairo_bsr* a, int32_t layout, int64_t
     case Path::kSplit:
       p.kernel = KAIRO_KERNEL_SPLIT_BF16;
       p.schedule = KAIRO_SCHEDULE_ROWS;
-      p.launches = 3;
+      p.launches = 2;
       p.grid = ch.plan.grid;
       p.n_tile = 128 * ch.plan.nt;
       p.stages = ch.plan.stages;

@@ -12,7 +12,7 @@
 //                        3c, 3c+1, 3c+2 for A's block-column c;
 //   block-row c of B  -> block-rows 3c, 3c+1, 3c+2 = (hi, lo, hi) of a
 //                        (3 * nbc * bk) x N bf16 B.
-// Two kernels build the derived operands in the caller's workspace; the
+// One kernel builds the derived operands in the caller's workspace; the
 // tcgen05 kernel then runs on them unchanged.
 #include <cuda_bf16.h>
 
@@ -54,18 +54,17 @@ __device__ __forceinline__ uint2 pack4(__nv_bfloat16 a, __nv_bfloat16 b, __nv_bf
 // column -1, which the tcgen05 kernel reports as KAIRO_DEVERR_BAD_INDEX; an
 // out-of-range block-column maps to an out-of-range derived column, reported
 // the same way.
-__global__ void k_split_blocks(const float* __restrict__ blocks, const int32_t* __restrict__ blk_idx,
-                               int64_t nblocks_stored, const int32_t* __restrict__ col_idx,
-                               const int32_t* __restrict__ row_ptr, int32_t nbr, int64_t nnzb, int32_t elems,
-                               __nv_bfloat16* __restrict__ out, int32_t* __restrict__ col_out,
-                               int32_t* __restrict__ row_ptr_out) {
-  const int64_t tstride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i <= nbr; i += tstride)
-    row_ptr_out[i] = 3 * row_ptr[i];
+__device__ void split_blocks_part(int64_t cta, int64_t ncta, const float* __restrict__ blocks,
+                                  const int32_t* __restrict__ blk_idx, int64_t nblocks_stored,
+                                  const int32_t* __restrict__ col_idx, const int32_t* __restrict__ row_ptr,
+                                  int32_t nbr, int64_t nnzb, int32_t elems, __nv_bfloat16* __restrict__ out,
+                                  int32_t* __restrict__ col_out, int32_t* __restrict__ row_ptr_out) {
+  const int64_t tstride = ncta * blockDim.x;
+  for (int64_t i = cta * blockDim.x + threadIdx.x; i <= nbr; i += tstride) row_ptr_out[i] = 3 * row_ptr[i];
   const int lane = threadIdx.x & 31;
   const int64_t warps = tstride / 32;
   const int vecs = elems / 4;
-  for (int64_t q = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; q < nnzb; q += warps) {
+  for (int64_t q = (cta * blockDim.x + threadIdx.x) / 32; q < nnzb; q += warps) {
     const int64_t blk = blk_idx ? static_cast<int64_t>(blk_idx[q]) : q;
     const int64_t c3 = 3 * static_cast<int64_t>(col_idx[q]);
     const bool in_store = blk >= 0 && blk < nblocks_stored;
@@ -97,12 +96,11 @@ __global__ void k_split_blocks(const float* __restrict__ blocks, const int32_t* 
 // index is divided.
 constexpr int kRowsPerPass = 4;
 
-__global__ void k_split_b(const float* __restrict__ b, int64_t ldb, int64_t k, int64_t n, int32_t bk, int64_t k_src,
-                          int64_t ldb_out, __nv_bfloat16* __restrict__ out) {
-  for (int64_t r0 = static_cast<int64_t>(blockIdx.y) * kRowsPerPass; r0 < k_src;
-       r0 += static_cast<int64_t>(gridDim.y) * kRowsPerPass) {
-    for (int64_t col = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; col < n;
-         col += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+__device__ void split_b_part(int64_t cx, int64_t ncx, int64_t cy, int64_t ncy, const float* __restrict__ b,
+                             int64_t ldb, int64_t k, int64_t n, int32_t bk, int64_t k_src, int64_t ldb_out,
+                             __nv_bfloat16* __restrict__ out) {
+  for (int64_t r0 = cy * kRowsPerPass; r0 < k_src; r0 += ncy * kRowsPerPass) {
+    for (int64_t col = cx * blockDim.x + threadIdx.x; col < n; col += ncx * blockDim.x) {
       float v[kRowsPerPass];
 #pragma unroll
       for (int u = 0; u < kRowsPerPass; ++u) {
@@ -122,6 +120,28 @@ __global__ void k_split_b(const float* __restrict__ b, int64_t ldb, int64_t k, i
         out[((3 * c + 2) * bk + kk) * ldb_out + col] = hi;
       }
     }
+  }
+}
+
+// Both splits in one launch: CTAs [0, nb_ctas) split the blocks, the rest
+// split B as a (bx_ctas x by_ctas) grid of column chunks x row groups.
+__global__ void __launch_bounds__(256) k_split(const float* __restrict__ blocks, const int32_t* __restrict__ blk_idx,
+                                               int64_t nblocks_stored, const int32_t* __restrict__ col_idx,
+                                               const int32_t* __restrict__ row_ptr, int32_t nbr, int64_t nnzb,
+                                               int32_t elems, __nv_bfloat16* __restrict__ blocks_out,
+                                               int32_t* __restrict__ col_out, int32_t* __restrict__ row_ptr_out,
+                                               const float* __restrict__ b, int64_t ldb, int64_t k, int64_t n,
+                                               int32_t bk, int64_t k_src, int64_t ldb_out,
+                                               __nv_bfloat16* __restrict__ b_out, int32_t nb_ctas, int32_t bx_ctas,
+                                               int32_t by_ctas) {
+  const int64_t cta = blockIdx.x;
+  if (cta < nb_ctas) {
+    split_blocks_part(cta, nb_ctas, blocks, blk_idx, nblocks_stored, col_idx, row_ptr, nbr, nnzb, elems, blocks_out,
+                      col_out, row_ptr_out);
+  } else {
+    const int64_t bc = cta - nb_ctas;
+    const int64_t cy = bc / bx_ctas;
+    split_b_part(bc - cy * bx_ctas, bx_ctas, cy, by_ctas, b, ldb, k, n, bk, k_src, ldb_out, b_out);
   }
 }
 
@@ -164,19 +184,17 @@ kairo_status split_bf16_prepare(const kairo_bsr* a, const void* b, int64_t ldb, 
                                 void* base, cudaStream_t s) {
   uint8_t* p = static_cast<uint8_t*>(base);
   const int32_t elems = a->bm * a->bk;
-  k_split_blocks<<<grid_for(std::max<int64_t>(a->nnzb * 32, a->nbr + 1), 256), 256, 0, s>>>(
+  const int64_t k_src = l.k / 3;  // nbc * bk source rows, the last slab zero-padded past K
+  const int nb_ctas = grid_for(std::max<int64_t>(a->nnzb * 32, a->nbr + 1), 256);
+  const int bx_ctas = static_cast<int>(std::min<int64_t>((n + 255) / 256, 64));
+  const int by_ctas = static_cast<int>(std::min<int64_t>((k_src + kRowsPerPass - 1) / kRowsPerPass, 148 * 4));
+  k_split<<<nb_ctas + bx_ctas * by_ctas, 256, 0, s>>>(
       static_cast<const float*>(a->blocks), a->blk_idx, a->nblocks_stored, a->col_idx, a->row_ptr, a->nbr, a->nnzb,
       elems, reinterpret_cast<__nv_bfloat16*>(p + l.blocks_off), reinterpret_cast<int32_t*>(p + l.col_idx_off),
-      reinterpret_cast<int32_t*>(p + l.row_ptr_off));
+      reinterpret_cast<int32_t*>(p + l.row_ptr_off), static_cast<const float*>(b), ldb, a->cols, n, a->bk, k_src,
+      l.ldb, reinterpret_cast<__nv_bfloat16*>(p + l.b_off), nb_ctas, bx_ctas, by_ctas);
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "launch of the split-bf16 block kernel");
-  const int64_t k_src = l.k / 3;  // nbc * bk source rows, the last slab zero-padded past K
-  const dim3 gb(static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 64)),
-                static_cast<unsigned>(std::min<int64_t>((k_src + kRowsPerPass - 1) / kRowsPerPass, 148 * 4)));
-  k_split_b<<<gb, 256, 0, s>>>(static_cast<const float*>(b), ldb, a->cols, n, a->bk, k_src, l.ldb,
-                               reinterpret_cast<__nv_bfloat16*>(p + l.b_off));
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "launch of the split-bf16 B kernel");
+  if (e != cudaSuccess) return cuda_fail(e, "launch of the split-bf16 kernel");
   return KAIRO_STATUS_SUCCESS;
 }
 

@@ -125,3 +125,21 @@ def test_sparse_scatter_grad_graph_replay():
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(holder["out"].cpu(), oracle.sparse_scatter_grad(grad2, active, batch2, n, d))
+
+
+def test_split_bf16_graph_replay():
+    # The opt-in split-bf16 path (split kernel + tcgen05 SpMM) captured and
+    # replayed with new B values.
+    p = generate(WorkloadSpec("g", torch.float32, 512, 512, 128, 16, 0.8), seed=7)
+    a = bsr_from_tiles(p.tiles.to(DEV), p.row_ids.to(DEV), p.col_ids.to(DEV), (512, 512))
+    b = p.b.to(DEV)
+    out = torch.empty(512, 128, dtype=torch.float32, device=DEV)
+    cfg = KernelConfig(kernel="split_bf16")
+    g = _capture(lambda: block_sparse_mm_bsr(a, b, out=out, config=cfg))
+    b2 = torch.randn(512, 128, generator=torch.Generator().manual_seed(11))
+    b.copy_(b2.to(DEV))
+    out.fill_(float("nan"))
+    g.replay()
+    torch.cuda.synchronize()
+    ref = oracle.spmm_tiles(p.tiles, p.row_ids, p.col_ids, b2, 512, 512, 128, 16)
+    assert rel_fro(out, ref) <= 1e-4
