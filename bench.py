@@ -131,19 +131,93 @@ def l2_gather_peak(flush: torch.Tensor) -> float | None:
     return out.value if st == 0 else None
 
 
-def load_traffic(workload: str) -> float | None:
-    """DRAM bytes per launch of the SpMM kernel for the full single-GPU
-    workload, from the committed ncu summary (profiles/traffic_<workload>.txt)."""
+def load_traffic(workload: str, n_gpus: int, plan: dict) -> float | None:
+    """DRAM bytes per launch of the SpMM kernel, from the committed ncu
+    summary profiles/traffic_<workload>.txt, but only when that capture was
+    taken of this very launch: the same number of GPUs and the same launch
+    plan (kernel, schedule, grid, n_tile, stages, group_blocks, rows), both
+    recorded in the file.  Anything else returns None: traffic is not
+    scaled from another shape."""
     p = ROOT / "profiles" / f"traffic_{workload}.txt"
     if not p.exists():
         return None
+    fields = {}
     for line in p.read_text().splitlines():
-        if line.startswith("dram_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1])
-            except ValueError:
-                return None
-    return None
+        if ":" in line:
+            key, val = line.split(":", 1)
+            fields[key.strip()] = val.strip()
+    try:
+        cap_plan = json.loads(fields.get("plan", "null"))
+        if int(fields.get("n_gpus", "0")) != n_gpus or not isinstance(cap_plan, dict):
+            return None
+        keys = ("kernel", "schedule", "grid", "n_tile", "stages", "group_blocks", "rows")
+        if any(cap_plan.get(k) != plan.get(k) for k in keys):
+            return None
+        return float(fields["dram_bytes_per_launch"])
+    except (KeyError, ValueError):
+        return None
+
+
+def compute_peak(spec, plan: dict, peaks: dict, peak_kind: str) -> tuple[float, str]:
+    """The arithmetic peak (TFLOP/s) of the kernel that runs: the measured
+    dense bf16 tensor-core figure (burst: one kernel timed alone) for the
+    tcgen05 kernels; for the fp32 CUDA-core kernel the nominal fp32 FMA peak
+    of the device (2 FLOP x 128 lanes x SMs x max SM clock), since no
+    measured figure exists for it."""
+    if plan.get("kernel") in ("tcgen05", "split_bf16"):
+        return float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])), peak_kind
+    props = torch.cuda.get_device_properties(torch.cuda.current_device())
+    mhz = float(peaks.get("sm_max_mhz", 1965.0))
+    return 2.0 * 128 * props.multi_processor_count * mhz * 1e6 / 1e12, "nominal fp32 CUDA-core peak"
+
+
+def strict_roofline(flop: float, strict: float, ms: float, tensor_tflops: float, hbm_gbs: float,
+                    compute_bound: str = "tensor") -> dict:
+    """Roofline fraction that cannot exceed 1 by construction: the bound is
+    whichever of FLOP / arithmetic peak and strict bytes / HBM bandwidth is
+    the longer, and the fraction is that time over the measured kernel time.
+    ``compute_bound`` names the arithmetic unit ("tensor", or "fp32" for
+    the CUDA-core kernel)."""
+    t_flop = flop / (tensor_tflops * 1e12)
+    t_mem = strict / (hbm_gbs * 1e9)
+    t = ms / 1e3
+    if t_flop >= t_mem:
+        return {"bound": compute_bound, "achieved": flop / t / 1e12, "peak": tensor_tflops, "unit": "TFLOP/s",
+                "frac": t_flop / t, "t_roof_ms": t_flop * 1e3, "strict_bytes": strict, "flop": flop}
+    return {"bound": "hbm", "achieved": strict / t / 1e9, "peak": hbm_gbs, "unit": "GB/s", "frac": t_mem / t,
+            "t_roof_ms": t_mem * 1e3, "strict_bytes": strict, "flop": flop}
+
+
+def check_output(a, b, out, linear: bool) -> dict:
+    """Compares the whole result of the timed launches with the oracle (the
+    reference's arithmetic on fp32-widened inputs) over every block-row of
+    this rank's shard: relative Frobenius error of the whole shard and the
+    largest relative error of one block-row.  A bf16 result is compared with
+    the oracle rounded to bf16.  The checker, run after the timed region."""
+    from oracle import oracle
+    from kairo_b200.workloads import block_row_errors, rel_fro_chunked
+
+    t0 = time.perf_counter()
+    m, k = a.shape
+    bh = b.cpu()
+    if linear:
+        bh = bh.t().contiguous()  # the shard's X rows (n x K) as B (K x n)
+    n = bh.shape[1]
+    ref = oracle.spmm_bsr_rows(a.row_ptr.cpu(), a.col_idx.cpu(), None if a.blk_idx is None else a.blk_idx.cpu(),
+                               a.blocks.cpu(), bh, m, k, n, list(range(a.nbr)))[:m]
+    got = out.cpu()
+    if linear:
+        got = got.t()
+    if got.dtype != torch.float32:
+        ref = ref.to(got.dtype).float()
+        got = got.float()
+    err = rel_fro_chunked(got, ref)
+    rows = block_row_errors(got, ref, a.block_size[0])
+    return {"rel_err": err, "max_block_row_rel_err": float(rows.max()) if rows.numel() else 0.0,
+            "block_rows": int(a.nbr), "tolerance": 1e-3, "seconds": time.perf_counter() - t0,
+            "oracle_threads": oracle.num_threads(),
+            "against": "oracle (reference arithmetic, fp32-widened inputs)" +
+                       ("; bf16 result vs oracle rounded to bf16" if out.dtype != torch.float32 else "")}
 
 
 def workload_spec(args):
@@ -190,27 +264,46 @@ def host_bsr(problem, a):
     b = problem.b.cpu()
     if problem.spec.layout == "linear":
         b = b.t().contiguous()
-    return (a.row_ptr.cpu(), a.col_idx.cpu(), a.blocks.cpu(), b)
+    blocks = a.blocks.cpu() if a.blk_idx is None else a.blocks[a.blk_idx.long()].cpu()
+    return (a.row_ptr.cpu(), a.col_idx.cpu(), blocks, b)
+
+
+def host_bsr_from_coo(problem):
+    """The same BSR matrix built on the host by the reference's convention
+    (stable argsort of the tile rows, row offsets from the counts), with the
+    oracle: no code of this package's native library is involved."""
+    from oracle import oracle
+
+    spec = problem.spec
+    perm, _, cols_s = oracle.sort_coo_by_row(problem.mask.indices[0], problem.mask.indices[1], spec.nbr)
+    rows_sorted = problem.mask.indices[0].cpu()[perm]
+    row_ptr = oracle.row_offsets(rows_sorted, spec.nbr).to(torch.int32)
+    tiles = problem.tiles.cpu()
+    blocks = tiles if torch.equal(perm, torch.arange(perm.numel())) else tiles[perm].contiguous()
+    b = problem.b.cpu()
+    if spec.layout == "linear":
+        b = b.t().contiguous()
+    return (row_ptr, cols_s.to(torch.int32), blocks, b)
 
 
 # ---------------------------------------------------------------- reference arm
 
 def run_reference(args) -> None:
+    """The reference's CPU algorithm for this path on the host cores.  The
+    workload is generated with plain torch on the GPU (the same seeded
+    inputs as our arm) and copied to the host; the BSR form is built on the
+    host by the oracle; the timed work is the oracle alone."""
     rank, world, local = dist_env()
     if rank != 0:
         return
     spec = workload_spec(args)
-    torch.cuda.set_device(local) if torch.cuda.is_available() else None
-    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    if not torch.cuda.is_available():
+        raise SystemExit("the reference arm generates its seeded workload on a CUDA device")
+    torch.cuda.set_device(local)
     t0 = time.perf_counter()
-    problem = generate(spec, seed=args.seed, device=dev)
-    from kairo_b200.ops import bsr_from_tiles
-
-    if dev == "cuda":
-        a = bsr_from_tiles(problem.tiles, problem.row_ids, problem.col_ids, (spec.m, spec.k))
-        host = host_bsr(problem, a)
-    else:
-        raise SystemExit("the reference arm needs the workload generated on a CUDA device")
+    problem = generate(spec, seed=args.seed, device="cuda")
+    torch.cuda.synchronize()
+    host = host_bsr_from_coo(problem)
     log(f"[reference] workload ready in {time.perf_counter() - t0:.1f}s")
     values, secs = [], []
     desc, threads = "", 0
@@ -336,13 +429,25 @@ def run_ours(args) -> None:
         dist.barrier()
     torch.cuda.synchronize()
     per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]  # ms
+    # The device error word of the workspace every timed launch used: a
+    # bad index or a timed-out wait in any of them leaves it nonzero.
+    from kairo_b200 import _lib
+
+    dev_err = _lib.read_workspace_error(_lib.workspace(0, dev), clear=True)
     l2_peak = l2_gather_peak(flush)
     total_ms = sum(per_step)
-    t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+    my_ms = total_ms / args.steps
+    mine = torch.tensor([my_ms, float(local_nnzb), float(dev_err)], dtype=torch.float64, device=dev)
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    job_ms = t.item()
+        every = torch.empty(world, 3, dtype=torch.float64, device=dev)
+        dist.all_gather_into_tensor(every, mine)
+    else:
+        every = mine.view(1, 3)
+    every = every.cpu()
+    rank_ms = every[:, 0].tolist()
+    job_ms = max(rank_ms) * args.steps
     ms_per_step = job_ms / args.steps
+    dev_errs = sorted({int(x) for x in every[:, 2].tolist()} - {0})
     total_flop = flops(spec)
     value = total_flop / (ms_per_step / 1e3) / 1e12
 
@@ -352,13 +457,22 @@ def run_ours(args) -> None:
     local_flop = flops(local_spec, nnzb=local_nnzb)
     local_canon = canonical_bytes(local_spec, nnzb=local_nnzb, nbr=a.nbr, m=local_rows)
     local_strict = strict_bytes(local_spec, nnzb=local_nnzb, nbr=a.nbr, m=local_rows)
-    my_ms = total_ms / args.steps
-    achieved = local_canon / (my_ms / 1e3) / 1e9
-    traffic_full = load_traffic(spec.name)
-    traffic = None
-    if traffic_full is not None:
-        traffic = traffic_full * (local_nnzb / max(1, a_full.nnzb)) * (ncols / spec.n)
-    bf16_peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    traffic = load_traffic(spec.name, world, plan)
+    tensor_peak, tensor_peak_kind = compute_peak(spec, plan, peaks, peak_kind)
+    roof = strict_roofline(local_flop, local_strict, my_ms, tensor_peak, hbm,
+                           "tensor" if plan.get("kernel") in ("tcgen05", "split_bf16") else "fp32")
+
+    # The checker: the whole output of the timed launches against the
+    # oracle (outside the timed region).  Each rank checks its own shard.
+    parity = None
+    if not args.no_check:
+        parity = check_output(a, b, out, linear)
+        pt = torch.tensor([parity["rel_err"], parity["max_block_row_rel_err"]], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(pt, op=dist.ReduceOp.MAX)
+        parity["rel_err"], parity["max_block_row_rel_err"] = pt.tolist()
+        parity["scope"] = ("every block-row and column of the output" if world == 1 else
+                           "every block-row and column of every rank's shard (max over ranks)")
 
     # Optional replicated output (reported separately, not part of the step).
     gather_ms = None
@@ -416,21 +530,28 @@ def run_ours(args) -> None:
                 "plan": plan,
             },
             "roofline": {
-                "bound": "hbm",
-                "achieved": achieved,
-                "peak": hbm,
-                "unit": "GB/s",
-                "frac": achieved / hbm,
+                **roof,
                 "traffic": traffic,
-                "peak_kind": peak_kind,
-                "bytes_definition": "canonical: A blocks + int32 indices + gathered B panel per block + C",
-                "strict_frac": local_strict / (my_ms / 1e3) / 1e9 / hbm,
-                "tensor_frac": local_flop / (my_ms / 1e3) / 1e12 / bf16_peak,
-                # The gathered panels are served by L2: the canonical bytes
-                # against this GPU's measured L2 -> SM bulk-copy ceiling.
+                "peak_kind": peak_kind if roof["bound"] == "hbm" else tensor_peak_kind,
+                "definition": ("max(FLOP / tensor peak, strict bytes / HBM bandwidth) for rank 0's shard, over "
+                               "its mean kernel time; strict bytes = A blocks + int32 indices + B once + C"),
+                "traffic_source": ("ncu capture of this launch plan (profiles/traffic_<workload>.txt)"
+                                   if traffic is not None else "no capture of this launch plan"),
+                # canonical bytes count one gathered B panel per block; most
+                # of those come from L2, so this fraction can exceed 1
+                "canonical_gbs": local_canon / (my_ms / 1e3) / 1e9,
+                "canonical_frac": local_canon / (my_ms / 1e3) / 1e9 / hbm,
+                # the same canonical bytes against this GPU's measured L2 -> SM
+                # bulk-copy ceiling (kairo_gather_probe), measured live
                 "l2_gather_peak_gbs": l2_peak,
-                "l2_frac": (achieved / l2_peak) if l2_peak else None,
+                "l2_frac": (local_canon / (my_ms / 1e3) / 1e9 / l2_peak) if l2_peak else None,
             },
+            "parity": parity,
+            "parity_rel_err": None if parity is None else parity["rel_err"],
+            "device_errors": dev_errs,
+            "ranks": {"kernel_ms_min": min(rank_ms), "kernel_ms_median": statistics.median(rank_ms),
+                      "kernel_ms_max": max(rank_ms), "nnzb_min": int(every[:, 1].min()),
+                      "nnzb_max": int(every[:, 1].max())},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": args.steps * plan["launches"],
@@ -621,6 +742,40 @@ def run_backward(args) -> None:
         "clocks": sampler.summary(),
     }
     print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- autotuner
+
+def run_tune(args) -> None:
+    """The autotuner's candidates on a named workload: every launch variant
+    of BLACKWELL_VARIANTS (plus the library default) timed on the actual
+    matrix by TileAutotuner.time_kernel_configs (CUDA events, median of
+    BENCH_ITERS, L2 not flushed between calls), and the one
+    best_kernel_config picks.  Evidence for the library's defaults."""
+    from kairo_b200.ops import TileAutotuner, bsr_from_tiles, describe
+
+    rank, world, local = dist_env()
+    if world > 1:
+        raise SystemExit("--op tune runs on one GPU")
+    torch.cuda.set_device(local)
+    spec = workload_spec(args)
+    if spec.layout == "linear":
+        raise SystemExit("--op tune times the STANDARD layout; the linear layer's X^T is its B")
+    problem = generate(spec, seed=args.seed, device="cuda")
+    a = bsr_from_tiles(problem.tiles, problem.row_ids, problem.col_ids, (spec.m, spec.k))
+    tuner = TileAutotuner()
+    rows = []
+    for kc, ms in tuner.time_kernel_configs(a, spec.n, B=problem.b):
+        try:
+            plan = describe(a, spec.n, config=kc)
+        except Exception as exc:  # noqa: BLE001 - a variant this shape does not support
+            plan = {"unsupported": str(exc)}
+        rows.append({"n_tile": kc.n_tile, "stages": kc.stages, "row_cost": kc.row_cost, "schedule": kc.schedule,
+                     "group_blocks": kc.group_blocks, "ms": ms, "tflops": flops(spec) / (ms / 1e3) / 1e12,
+                     "plan": plan})
+    best = tuner.best_kernel_config(a, spec.n)
+    print(json.dumps({"op": "tune", "workload": spec.name, "candidates": rows,
+                      "best": dataclasses.asdict(best), "default_plan": describe(a, spec.n)}), flush=True)
 
 
 # ---------------------------------------------------------------- block pruning
@@ -924,9 +1079,11 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-check", action="store_true",
+                    help="skip the check of the timed launches' output against the oracle")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=3.0)
-    ap.add_argument("--op", choices=("spmm", "backward", "prune", "gather", "scatter"), default="spmm",
+    ap.add_argument("--op", choices=("spmm", "backward", "prune", "gather", "scatter", "tune"), default="spmm",
                     help="spmm (default): the block-sparse SpMM; backward: the linear layer's dX and dW; "
                          "prune: block norms + top-k of the linear layer's weight; "
                          "gather/scatter: the masked embedding ops")
@@ -939,6 +1096,8 @@ def main() -> None:
             raise SystemExit("--impl reference times the SpMM path only")
         if args.op == "backward":
             run_backward(args)
+        elif args.op == "tune":
+            run_tune(args)
         elif args.op == "prune":
             run_prune(args)
         else:

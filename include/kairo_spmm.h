@@ -79,6 +79,12 @@ typedef enum kairo_kernel {
 #define KAIRO_DEVERR_WAIT_TIMEOUT 1u      /* a pipeline wait ran out; the kernel stopped */
 #define KAIRO_DEVERR_BAD_INDEX 2u         /* a tile row/column id outside the block grid */
 #define KAIRO_DEVERR_ROW_TOO_LONG 3u      /* unsorted COO with a block-row longer than the sort limit */
+/* Site tags of KAIRO_DEVERR_WAIT_TIMEOUT (bits 8..15): which wait ran out. */
+#define KAIRO_WAIT_SITE_EMPTY 1u          /* producer waiting for a free shared-memory stage */
+#define KAIRO_WAIT_SITE_FULL 2u           /* MMA issuer waiting for a loaded stage */
+#define KAIRO_WAIT_SITE_TMEM_EMPTY 3u     /* MMA issuer waiting for a drained TMEM accumulator */
+#define KAIRO_WAIT_SITE_TMEM_FULL 4u      /* epilogue waiting for a finished accumulator */
+#define KAIRO_WAIT_SITE_DRAIN 5u          /* a CTA draining its copies or MMAs before it exits */
 
 /* Block-sparse matrix in BSR form (all pointers are device pointers). */
 typedef struct kairo_bsr {
@@ -108,7 +114,15 @@ typedef struct kairo_spmm_config {
   int32_t group_blocks;      /* nonzero blocks per pipeline stage, 1..32 (0 = auto) */
   int32_t schedule;          /* kairo_schedule (tcgen05 kernel only) */
   int32_t band_rows;         /* block-rows per item of the band schedule (0 = auto) */
-  int32_t reserved[4];
+  int32_t wait_kcycles;      /* bound of every pipeline wait of the tcgen05 kernels, in thousands of SM
+                                cycles (0 = the default, 8e9 cycles, about 4 s); a debugging knob */
+  int32_t debug_hold_stage;  /* test hook, 0 in normal use.  1: the row-split kernel's producer holds
+                                back the arrival of its first pipeline stage until the kernel aborts
+                                (bounded by 4 wait bounds), so that a consumer's bounded wait runs out:
+                                the launch records KAIRO_DEVERR_WAIT_TIMEOUT with the wait's site tag,
+                                drains its copies and MMAs, frees TMEM and returns.  Ignored by the other
+                                kernels. */
+  int32_t reserved[2];
 } kairo_spmm_config;
 
 /* Work schedules of the tcgen05 kernel.

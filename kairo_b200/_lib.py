@@ -54,6 +54,13 @@ DEVERR_WAIT_TIMEOUT = 1
 DEVERR_BAD_INDEX = 2
 DEVERR_ROW_TOO_LONG = 3
 
+# wait-site tags of DEVERR_WAIT_TIMEOUT (bits 8..15)
+WAIT_SITE_EMPTY = 1
+WAIT_SITE_FULL = 2
+WAIT_SITE_TMEM_EMPTY = 3
+WAIT_SITE_TMEM_FULL = 4
+WAIT_SITE_DRAIN = 5
+
 _TORCH_TO_KAIRO = {torch.float32: DTYPE_F32, torch.float16: DTYPE_F16, torch.bfloat16: DTYPE_BF16}
 
 
@@ -86,7 +93,9 @@ class KairoSpmmConfig(Structure):
         ("group_blocks", c_int32),
         ("schedule", c_int32),
         ("band_rows", c_int32),
-        ("reserved", c_int32 * 4),
+        ("wait_kcycles", c_int32),
+        ("debug_hold_stage", c_int32),
+        ("reserved", c_int32 * 2),
     ]
 
 
@@ -272,3 +281,37 @@ def raise_on_device_error(ws: torch.Tensor) -> None:
     code = read_workspace_error(ws, clear=True)
     if code:
         raise KairoDeviceError(code)
+
+
+class KairoDeviceWarning(RuntimeWarning):
+    """A device error that an earlier, unchecked launch left in a workspace."""
+
+
+def take_pending_error(ws: torch.Tensor, where: str) -> int:
+    """Reads and clears the error word of a cached workspace before a launch
+    whose own errors the caller asked to see (``check=True``).  An error
+    found there was recorded by an earlier launch made with ``check=False``
+    on the same stream; it is reported as a :class:`KairoDeviceWarning`
+    naming it as such, so that the error read after the checked launch
+    belongs to that launch alone.  Returns the earlier code (0 if none)."""
+    code = read_workspace_error(ws, clear=True)
+    if code:
+        import warnings
+
+        warnings.warn(KairoDeviceWarning(f"{where}: an earlier launch with check=False on this stream recorded "
+                                         f"{KairoDeviceError(code)}; cleared before this launch"), stacklevel=3)
+    return code
+
+
+def pending_device_error(device: torch.device | int | None = None, clear: bool = True) -> int:
+    """The device error word of the cached workspace of ``device``'s current
+    stream: what launches made with ``check=False`` there have recorded
+    since it was last read (KAIRO_DEVERR_* in the low 8 bits, the wait site
+    above them; 0 = none).  Synchronises that stream."""
+    if device is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    elif isinstance(device, int):
+        dev = torch.device("cuda", device)
+    else:
+        dev = torch.device(device)
+    return read_workspace_error(workspace(0, dev), clear=clear)

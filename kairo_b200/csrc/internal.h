@@ -71,6 +71,8 @@ struct TcPlan {
   size_t counters_offset, counters_bytes;
   size_t partials_offset, partials_bytes;
   size_t workspace_bytes;
+  long long wait_cycles;   // bound of every mbarrier wait (kairo_spmm_config.wait_kcycles)
+  int hold_stage;          // kairo_spmm_config.debug_hold_stage
 };
 
 // TMA tensor maps (tma_maps.cu).  make_operand_maps builds the block-storage
@@ -103,6 +105,7 @@ struct BandPlan {
   size_t smem_bytes;
   size_t order_offset, order_bytes;
   size_t workspace_bytes;
+  long long wait_cycles;   // bound of every mbarrier wait (kairo_spmm_config.wait_kcycles)
 };
 
 // Band schedule (spmm_band.cu)

@@ -72,6 +72,7 @@ struct BandArgs {
   uint32_t tmem_cols;
   int32_t vec_store;
   int32_t b_box3d;
+  long long wait_cycles;  // bound of every mbarrier wait
 };
 
 // ------------------------------------------------------------ column order
@@ -331,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         while (j0 < cnt) {
           const int take = min(GB - gpos, cnt - j0);
           if (gpos == 0) {
-            int ok = ptx::wait_parity(&empty[gidx], gph ^ 1u, abort_flag, args.err, kTagEmpty, kWaitCycles);
+            int ok = ptx::wait_parity(&empty[gidx], gph ^ 1u, abort_flag, args.err, kTagEmpty, args.wait_cycles);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) {
               alive = false;
@@ -417,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int buf = static_cast<int>(nonempty % NSLOT);
       const uint32_t ph = static_cast<uint32_t>((nonempty / NSLOT) & 1);
       ++nonempty;
-      int ok = ptx::wait_parity(&tempty[buf], ph ^ 1u, abort_flag, args.err, kTagTmemEmpty, kWaitCycles);
+      int ok = ptx::wait_parity(&tempty[buf], ph ^ 1u, abort_flag, args.err, kTagTmemEmpty, args.wait_cycles);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       ptx::tc_fence_after();
@@ -426,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int i = 0;
       while (i < total) {
         if (mpos == 0) {
-          ok = ptx::wait_parity(&full[midx], mph, abort_flag, args.err, kTagFull, kWaitCycles);
+          ok = ptx::wait_parity(&full[midx], mph, abort_flag, args.err, kTagFull, args.wait_cycles);
           ok = __shfl_sync(0xffffffffu, ok, 0);
           if (!ok) {
             alive = false;
@@ -469,7 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (mpos != 0) ptx::mma_commit_if(leader, &empty[midx]);
     ptx::mma_commit_if(leader, mma_done);
     int dummy = 0;
-    ptx::wait_parity(mma_done, 0, reinterpret_cast<volatile int*>(&dummy), args.err, kTagDrain, kWaitCycles);
+    ptx::wait_parity(mma_done, 0, reinterpret_cast<volatile int*>(&dummy), args.err, kTagDrain, args.wait_cycles);
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
@@ -495,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int buf = static_cast<int>(nonempty % NSLOT);
       const uint32_t ph = static_cast<uint32_t>((nonempty / NSLOT) & 1);
       ++nonempty;
-      int ok = ptx::wait_parity(&tfull[buf], ph, abort_flag, args.err, kTagTmemFull, kWaitCycles, 200);
+      int ok = ptx::wait_parity(&tfull[buf], ph, abort_flag, args.err, kTagTmemFull, args.wait_cycles, 200);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (epi_any(!ok)) break;
       ptx::tc_fence_after();
@@ -533,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < S; ++s)
       if (issued[s])
         ptx::wait_parity(&full[s], static_cast<uint32_t>(issued[s] - 1), reinterpret_cast<volatile int*>(&dummy),
-                         args.err, kTagDrain, kWaitCycles);
+                         args.err, kTagDrain, args.wait_cycles);
   }
   __syncthreads();
   if (warp == 1) {
@@ -656,6 +657,8 @@ kairo_status band_plan(const kairo_bsr* a, int32_t layout, int64_t n, const kair
   if (grid < 1) grid = 1;
   p.grid = static_cast<int>(grid);
   p.serpentine = 1;
+  if (cfg && cfg->wait_kcycles < 0) return fail(KAIRO_STATUS_INVALID_VALUE, "wait_kcycles must be >= 0");
+  p.wait_cycles = wait_bound_cycles(cfg);
   const int sb = stage_bytes(p.bm, p.bk, nt);
   int group = (cfg && cfg->group_blocks > 0) ? cfg->group_blocks : 0;
   if (group > 32) return fail(KAIRO_STATUS_INVALID_VALUE, "group_blocks must be at most 32");
@@ -718,6 +721,7 @@ kairo_status band_launch(const kairo_bsr* a, const void* b, int64_t ldb, int32_t
   args.serpentine = plan.serpentine;
   args.tmem_cols = plan.tmem_cols;
   args.b_box3d = b_box3d;
+  args.wait_cycles = plan.wait_cycles;
   const size_t osz = c_dtype == KAIRO_DTYPE_F32 ? 4 : 2;
   args.vec_store = linear && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0) && ((ldc * osz) % 16 == 0) ? 1 : 0;
 

@@ -32,8 +32,11 @@ __device__ __forceinline__ void split_bf16(float v, __nv_bfloat16* hi, __nv_bflo
   *lo = isfinite(hf) ? __float2bfloat16_rn(v - hf) : __float2bfloat16_rn(0.f);
 }
 
+// CTAs for `items` threads of work: at most 8 resident CTAs per SM of the
+// current device.
 int grid_for(int64_t items, int threads) {
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((items + threads - 1) / threads, 148 * 8)));
+  const int64_t cap = static_cast<int64_t>(device_sm_count(current_device())) * 8;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((items + threads - 1) / threads, cap)));
 }
 
 __device__ __forceinline__ uint2 pack4(__nv_bfloat16 a, __nv_bfloat16 b, __nv_bfloat16 c, __nv_bfloat16 d) {
@@ -187,7 +190,8 @@ kairo_status split_bf16_prepare(const kairo_bsr* a, const void* b, int64_t ldb, 
   const int64_t k_src = l.k / 3;  // nbc * bk source rows, the last slab zero-padded past K
   const int nb_ctas = grid_for(std::max<int64_t>(a->nnzb * 32, a->nbr + 1), 256);
   const int bx_ctas = static_cast<int>(std::min<int64_t>((n + 255) / 256, 64));
-  const int by_ctas = static_cast<int>(std::min<int64_t>((k_src + kRowsPerPass - 1) / kRowsPerPass, 148 * 4));
+  const int by_ctas = static_cast<int>(std::min<int64_t>((k_src + kRowsPerPass - 1) / kRowsPerPass,
+                                                          static_cast<int64_t>(device_sm_count(current_device())) * 4));
   k_split<<<nb_ctas + bx_ctas * by_ctas, 256, 0, s>>>(
       static_cast<const float*>(a->blocks), a->blk_idx, a->nblocks_stored, a->col_idx, a->row_ptr, a->nbr, a->nnzb,
       elems, reinterpret_cast<__nv_bfloat16*>(p + l.blocks_off), reinterpret_cast<int32_t*>(p + l.col_idx_off),

@@ -78,6 +78,8 @@ struct TcArgs {
   uint32_t tmem_cols;      // TMEM columns allocated (power of two, >= 2*NT*BM)
   int32_t vec_store;       // LINEAR: rows of Y may be written with 16-byte stores
   int32_t b_box3d;         // STANDARD: the whole B panel is one 3D box (N % 64 == 0)
+  int32_t hold_stage;      // test hook: hold back the first stage's arrival until the kernel aborts
+  long long wait_cycles;   // bound of every mbarrier wait
 };
 
 struct RowItem {
@@ -277,6 +279,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     int gidx = 0;      // stage of the current group
     uint32_t gph = 0;  // phase of that stage
     IndexWindow win;
+    // Test hook (args.hold_stage): the first stage's arrival waits until a
+    // consumer's bounded wait has run out and set the abort flag, or for
+    // four wait bounds at most; then it arrives, so that the stage's phase
+    // completes once its loads have landed and the drain below finds them.
+    bool held = args.hold_stage == 0;
+    auto hold_first_arrival = [&]() {
+      if (held) return;
+      held = true;
+      const long long t0 = clock64();
+      while (!*abort_flag && clock64() - t0 < 4 * args.wait_cycles) __nanosleep(256);
+      __syncwarp();
+    };
     walk_items(args, s_range, e_range, i_start, lane, [&](const RowItem& it) -> bool {
       if (it.kind != kDirect && it.kind != kPartial) return true;
       const int n0 = it.chunk * NT * 128;
@@ -300,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         while (j0 < cnt) {
           const int take = min(GB - gpos, cnt - j0);
           if (gpos == 0) {
-            int ok = ptx::wait_parity(&empty[gidx], gph ^ 1u, abort_flag, args.err, kTagEmpty, kWaitCycles);
+            int ok = ptx::wait_parity(&empty[gidx], gph ^ 1u, abort_flag, args.err, kTagEmpty, args.wait_cycles);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) return false;
             if (lane == 0) issued[gidx] = static_cast<int>(gph) + 1;
@@ -325,6 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           gpos += take;
           j0 += take;
           if (gpos == GB) {
+            hold_first_arrival();
             ptx::mbar_arrive_if(leader, &full[gidx]);
             gpos = 0;
             if (++gidx == S) {
@@ -338,7 +353,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     });
     // Close a partly filled last group (also after an abort, so that the
     // loads already issued can complete its phase before the drain below).
-    if (gpos != 0) ptx::mbar_arrive_if(leader, &full[gidx]);
+    if (gpos != 0) {
+      hold_first_arrival();
+      ptx::mbar_arrive_if(leader, &full[gidx]);
+    }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -361,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t slot16 = 0;  // (byte offset of the current block slot) >> 4
     walk_items(args, s_range, e_range, i_start, lane, [&](const RowItem& it) -> bool {
       if (it.kind != kDirect && it.kind != kPartial) return true;
-      int ok = ptx::wait_parity(&tempty[slot], aphase ^ 1u, abort_flag, args.err, kTagTmemEmpty, kWaitCycles);
+      int ok = ptx::wait_parity(&tempty[slot], aphase ^ 1u, abort_flag, args.err, kTagTmemEmpty, args.wait_cycles);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) return false;
       ptx::tc_fence_after();
@@ -371,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (mpos == 0) {
           // No tcgen05 fence here: the MMAs read shared memory the TMA wrote,
           // and the mbarrier wait itself orders them after those writes.
-          ok = ptx::wait_parity(&full[midx], mph, abort_flag, args.err, kTagFull, kWaitCycles);
+          ok = ptx::wait_parity(&full[midx], mph, abort_flag, args.err, kTagFull, args.wait_cycles);
           ok = __shfl_sync(0xffffffffu, ok, 0);
           if (!ok) return false;
           slot16 = static_cast<uint32_t>(midx * GB) * SLOT16;
@@ -412,7 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (mpos != 0) ptx::mma_commit_if(leader, &empty[midx]);
     ptx::mma_commit_if(leader, mma_done);
     int dummy = 0;
-    ptx::wait_parity(mma_done, 0, reinterpret_cast<volatile int*>(&dummy), args.err, kTagDrain, kWaitCycles);
+    ptx::wait_parity(mma_done, 0, reinterpret_cast<volatile int*>(&dummy), args.err, kTagDrain, args.wait_cycles);
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
@@ -433,7 +451,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j0 = 0; j0 < BM; j0 += 16) store16<LINEAR, TOut>(args, it.row, BM, j0, n0 + t * 128 + e, z);
         return true;
       }
-      int ok = ptx::wait_parity(&tfull[slot], aphase, abort_flag, args.err, kTagTmemFull, kWaitCycles, 200);
+      int ok = ptx::wait_parity(&tfull[slot], aphase, abort_flag, args.err, kTagTmemFull, args.wait_cycles, 200);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (epi_any(!ok)) return false;
       ptx::tc_fence_after();
@@ -501,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < S; ++s)
       if (issued[s])
         ptx::wait_parity(&full[s], static_cast<uint32_t>(issued[s] - 1), reinterpret_cast<volatile int*>(&dummy),
-                         args.err, kTagDrain, kWaitCycles);
+                         args.err, kTagDrain, args.wait_cycles);
   }
   __syncthreads();
   if (warp == 1) {
@@ -551,10 +569,18 @@ KernelFn pick_kernel(int bm, int nt, bool linear, kairo_dtype in, kairo_dtype ou
 size_t elem_size(kairo_dtype d) { return d == KAIRO_DTYPE_F32 ? 4 : 2; }
 
 // Counter bank of the next launch on `workspace` (alternates per workspace).
+// The map is bounded: past kMaxTrackedWorkspaces entries it is cleared, and
+// the next launch on a forgotten workspace uses bank 0.  That is safe after
+// a launch that completed, which leaves both banks at zero (it zeroed the
+// other bank and reset its own counters).  Only after an aborted launch
+// (a recorded device error) can bank 0 still hold counters, which is why
+// the banks alternate at all.
 int next_counter_bank(void* workspace) {
+  constexpr size_t kMaxTrackedWorkspaces = 4096;
   static std::mutex mu;
   static std::unordered_map<void*, int> parity;
   std::lock_guard<std::mutex> lock(mu);
+  if (parity.size() >= kMaxTrackedWorkspaces && parity.find(workspace) == parity.end()) parity.clear();
   int& b = parity[workspace];
   const int use = b;
   b ^= 1;
@@ -609,6 +635,10 @@ kairo_status tc_plan(const kairo_bsr* a, int32_t layout, int64_t n, const kairo_
   // masks with many short or empty rows (measured on a Zipf(1.1) mask: the
   // slowest CTA finished 80 % after the median with weight 2, 6 % with 8).
   p.row_cost = (cfg && cfg->row_cost > 0) ? cfg->row_cost : 8;
+  if (cfg && (cfg->wait_kcycles < 0 || cfg->debug_hold_stage < 0 || cfg->debug_hold_stage > 1))
+    return fail(KAIRO_STATUS_INVALID_VALUE, "wait_kcycles must be >= 0 and debug_hold_stage 0 or 1");
+  p.wait_cycles = wait_bound_cycles(cfg);
+  p.hold_stage = (cfg && cfg->debug_hold_stage) ? 1 : 0;
   p.w = a->nnzb + static_cast<int64_t>(p.row_cost) * a->nbr;
   const int sms = device_sm_count(device);
   int grid = (cfg && cfg->num_ctas > 0) ? cfg->num_ctas : sms;
@@ -694,6 +724,8 @@ kairo_status tc_launch(const kairo_bsr* a, const void* b, int64_t ldb, int32_t l
   args.tmem_cols = plan.tmem_cols;
   const size_t osz = elem_size(c_dtype);
   args.b_box3d = b_box3d;
+  args.hold_stage = plan.hold_stage;
+  args.wait_cycles = plan.wait_cycles;
   args.vec_store = linear && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0) && ((ldc * osz) % 16 == 0) ? 1 : 0;
 
   cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -8,14 +8,29 @@
 
 #include <cstdint>
 
+#include "../../include/kairo_spmm.h"
+
 namespace kairo {
 
 constexpr int kThreads = 192;                    // warp 0 producer, warp 1 MMA, warps 2..5 epilogue
 constexpr long long kWaitCycles = 8000000000LL;  // per-wait bound in SM cycles (about 4 s at 2 GHz)
 constexpr int kMaxSmem = 227 * 1024;
 
-// Wait-site tags recorded with a timeout (bits 8..15 of the error word).
-enum : uint32_t { kTagEmpty = 1, kTagFull = 2, kTagTmemEmpty = 3, kTagTmemFull = 4, kTagDrain = 5 };
+// Wait-site tags recorded with a timeout (bits 8..15 of the error word),
+// the KAIRO_WAIT_SITE_* values of the C ABI.
+enum : uint32_t {
+  kTagEmpty = KAIRO_WAIT_SITE_EMPTY,
+  kTagFull = KAIRO_WAIT_SITE_FULL,
+  kTagTmemEmpty = KAIRO_WAIT_SITE_TMEM_EMPTY,
+  kTagTmemFull = KAIRO_WAIT_SITE_TMEM_FULL,
+  kTagDrain = KAIRO_WAIT_SITE_DRAIN
+};
+
+// Wait bound of a launch: the config's wait_kcycles (thousands of cycles)
+// or the default.
+inline long long wait_bound_cycles(const kairo_spmm_config* cfg) {
+  return (cfg && cfg->wait_kcycles > 0) ? static_cast<long long>(cfg->wait_kcycles) * 1000LL : kWaitCycles;
+}
 
 // Bytes of one pipeline slot: the B panel (NT sub-tiles of 128 x bk) and the
 // block (bm x bk), the block padded to 1 KiB for its swizzle atom.

@@ -25,6 +25,7 @@ from kairo_b200.ops.spmm import (
     bsr_from_mask,
     bsr_from_tiles,
     describe,
+    pending_device_error,
     sparse_linear,
 )
 
@@ -46,6 +47,7 @@ __all__ = [
     "bsr_from_mask",
     "bsr_from_tiles",
     "describe",
+    "pending_device_error",
     "sparse_linear",
     "KernelConfig",
     "BlockSparseLinear",

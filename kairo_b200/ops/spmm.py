@@ -36,7 +36,11 @@ class KernelConfig:
     nonzero blocks loaded per pipeline stage (1..32); schedule: "auto",
     "rows" (block-rows split over CTAs, robust to skew) or "bands" (CTAs
     sweep B panels together, for a B slice larger than L2); band_rows:
-    block-rows per band item.
+    block-rows per band item.  Debugging knobs: wait_kcycles bounds every
+    pipeline wait of the tcgen05 kernels (thousands of SM cycles; 0 = the
+    default of about 4 s); debug_hold_stage=1 (a test hook) makes the
+    row-split kernel hold back its first stage so that a bounded wait runs
+    out and the launch reports a wait timeout instead of computing C.
     """
 
     kernel: str = "auto"
@@ -47,6 +51,8 @@ class KernelConfig:
     group_blocks: int = 0
     schedule: str = "auto"
     band_rows: int = 0
+    wait_kcycles: int = 0
+    debug_hold_stage: int = 0
 
     def __post_init__(self) -> None:
         if self.kernel not in ("auto", "simt", "tcgen05", "split_bf16"):
@@ -55,7 +61,9 @@ class KernelConfig:
             raise ValueError(f"n_tile must be 0, 128 or 256, got {self.n_tile}")
         if self.schedule not in ("auto", "rows", "bands"):
             raise ValueError(f"schedule must be 'auto', 'rows' or 'bands', got {self.schedule!r}")
-        for name in ("stages", "row_cost", "num_ctas", "group_blocks", "band_rows"):
+        if self.debug_hold_stage not in (0, 1):
+            raise ValueError("debug_hold_stage must be 0 or 1")
+        for name in ("stages", "row_cost", "num_ctas", "group_blocks", "band_rows", "wait_kcycles"):
             if getattr(self, name) < 0:
                 raise ValueError(f"{name} must be non-negative")
         if self.group_blocks > 32:
@@ -72,7 +80,16 @@ class KernelConfig:
         c.group_blocks = self.group_blocks
         c.schedule = {"auto": _lib.SCHEDULE_AUTO, "rows": _lib.SCHEDULE_ROWS, "bands": _lib.SCHEDULE_BANDS}[self.schedule]
         c.band_rows = self.band_rows
+        c.wait_kcycles = self.wait_kcycles
+        c.debug_hold_stage = self.debug_hold_stage
         return c
+
+
+def pending_device_error(device: torch.device | int | None = None, clear: bool = True) -> int:
+    """Device error word left by ``check=False`` launches on ``device``'s
+    current stream (0 = none; KAIRO_DEVERR_* in the low 8 bits, the wait
+    site above).  Synchronises that stream; ``clear`` resets the word."""
+    return _lib.pending_device_error(device, clear)
 
 
 def _require_cuda(*tensors: Tensor, op: str) -> None:
@@ -251,6 +268,8 @@ def _launch(a: BlockSparseMatrix, b: Tensor, ldb: int, layout: int, n: int, out:
         _lib.check(lib.kairo_bsr_spmm_workspace_size(ctypes.byref(desc), layout, n, ctypes.byref(cfg),
                                                      ctypes.byref(nbytes)), "kairo_bsr_spmm")
         ws = _lib.workspace(nbytes.value, dev)
+        if check_device:
+            _lib.take_pending_error(ws, "kairo_bsr_spmm")
         _lib.check(lib.kairo_bsr_spmm(ctypes.byref(desc), b.data_ptr(), ldb, layout, n, out.data_ptr(), ldc,
                                       _lib.kairo_dtype(out.dtype), ctypes.byref(cfg), ws.data_ptr(), ws.numel(),
                                       _lib.stream_handle(dev)), "kairo_bsr_spmm")
@@ -270,7 +289,11 @@ def block_sparse_mm_bsr(
 
     Every element of C is written.  ``check=True`` synchronises and raises
     :class:`~kairo_b200._lib.KairoDeviceError` if the device recorded an
-    error (an out-of-range block index or a pipeline wait that timed out).
+    error in this launch (an out-of-range block index or a pipeline wait
+    that timed out).  With ``check=False`` (asynchronous) such errors stay
+    in the stream's workspace until :func:`pending_device_error` reads them;
+    the next ``check=True`` launch takes them out first and reports them as
+    a :class:`~kairo_b200._lib.KairoDeviceWarning`, not as its own.
     """
     _require_cuda(a.blocks, B, op="block_sparse_mm_bsr")
     m, k = a.shape

@@ -245,3 +245,44 @@ def roofline_time(flop: float, nbytes: float, tflops: float, gbs: float) -> floa
     """max(FLOP / peak, bytes / bandwidth) in seconds."""
     return max(flop / (tflops * 1e12), nbytes / (gbs * 1e9))
 
+
+
+# ------------------------------------------------------------------ checking
+
+def block_row_errors(c: torch.Tensor, ref: torch.Tensor, bm: int, chunk_rows: int = 1 << 16) -> torch.Tensor:
+    """Relative Frobenius error of every block-row of ``c`` against ``ref``.
+
+    Both are (M, N); block-row i is rows i*bm .. (i+1)*bm.  Computed on the
+    host in float64, ``chunk_rows`` rows at a time, so that a 262144 x 1024
+    result needs no float64 copy of the whole matrix.  A block-row whose
+    reference is all zero reports its absolute error norm instead.
+    Returns a float64 tensor of ceil(M / bm) errors.
+    """
+    if c.shape != ref.shape:
+        raise ValueError(f"shape mismatch {tuple(c.shape)} vs {tuple(ref.shape)}")
+    m = c.shape[0]
+    nbr = (m + bm - 1) // bm
+    num = torch.zeros(nbr, dtype=torch.float64)
+    den = torch.zeros(nbr, dtype=torch.float64)
+    step = max(bm, chunk_rows // bm * bm)
+    for r0 in range(0, m, step):
+        r1 = min(m, r0 + step)
+        x = c[r0:r1].detach().to("cpu", torch.float64)
+        y = ref[r0:r1].detach().to("cpu", torch.float64)
+        d2 = (x - y).square().sum(dim=1)
+        y2 = y.square().sum(dim=1)
+        rows = torch.arange(r0, r1) // bm
+        num.index_add_(0, rows, d2)
+        den.index_add_(0, rows, y2)
+    return torch.where(den > 0, (num / den.clamp_min(1e-300)).sqrt(), num.sqrt())
+
+
+def rel_fro_chunked(c: torch.Tensor, ref: torch.Tensor, chunk_rows: int = 1 << 16) -> float:
+    """||c - ref||_F / ||ref||_F in float64, ``chunk_rows`` rows at a time."""
+    num = den = 0.0
+    for r0 in range(0, c.shape[0], chunk_rows):
+        x = c[r0:r0 + chunk_rows].detach().to("cpu", torch.float64)
+        y = ref[r0:r0 + chunk_rows].detach().to("cpu", torch.float64)
+        num += float((x - y).square().sum())
+        den += float(y.square().sum())
+    return (num / den) ** 0.5 if den > 0 else num ** 0.5

@@ -1,7 +1,7 @@
 """Generates the golden fixtures of the SpMM path from the reference itself.
 
 Usage (needs the reference source tree; run where it is mounted):
-    python tests/golden/make_golden.py --ref /root/reference
+    python tests/golden/make_golden.py --ref <path of the reference source tree>
 
 The script imports the reference's own ``kairo`` package (its pure-PyTorch CPU
 path) and records, for seeded inputs:
@@ -83,7 +83,7 @@ def _record(spmm, se, ktypes, name, *, mask, tile, M, K, N, B, A=None, tiles=Non
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="path of the reference source tree (read-only)")
     args = ap.parse_args()
     spmm, se, ktypes = _ref_modules(Path(args.ref))
     sys.path.insert(0, str(REPO))

@@ -1,7 +1,7 @@
 """Generates the golden fixtures of the masked-embedding path from the reference.
 
 Usage (needs the reference source tree; run where it is mounted):
-    python tests/golden/make_golden_embedding.py --ref /root/reference
+    python tests/golden/make_golden_embedding.py --ref <path of the reference source tree>
 
 Imports the reference's own ``kairo.ops.sparse_embedding`` (its PyTorch path:
 ``kairo._C`` is not built, so ``sparse_gather`` / ``sparse_scatter_grad`` run
@@ -56,7 +56,7 @@ def _scatter_case(se, name, grad, active, batch, n, d):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="path of the reference source tree (read-only)")
     args = ap.parse_args()
     se, kt = _ref(Path(args.ref))
 
