@@ -168,13 +168,22 @@ KAIRO_API kairo_status kairo_bsr_spmm(const kairo_bsr* a, const void* b, int64_t
  * built into the library, one per device: every GPU that loads the library
  * holds it until the process exits.  Problems needing more scratch than that
  * return KAIRO_STATUS_NOT_SUPPORTED.  The first call on a device looks up the
- * array's device address (make it before any stream capture).  Each call
- * clears the array's error word and counters on `stream`.  Calls share the
- * array, so calls whose launches overlap on the GPU race: order them. */
+ * array's device address (make it before any stream capture); the address is
+ * cached per device and CUDA context, and looked up again under a new
+ * context.  Each call clears the array's error word and counters on
+ * `stream`.  Calls share the array, so calls whose launches overlap on the
+ * GPU race: order them. */
 KAIRO_API kairo_status kairo_bsr_spmm_noalloc(const kairo_bsr* a, const void* b, int64_t ldb,
                                               int32_t layout, int64_t n, void* c, int64_t ldc,
                                               kairo_dtype c_dtype, const kairo_spmm_config* cfg,
                                               void* stream);
+
+/* The device error word of the last kairo_bsr_spmm_noalloc call on the
+ * current device (KAIRO_DEVERR_* in the low 8 bits, a site tag above), read
+ * like kairo_workspace_error: synchronises `stream`, optionally clears the
+ * word.  Read it after a call and before the next one, which clears it.  No
+ * counterpart in the reference.  Allocates nothing. */
+KAIRO_API kairo_status kairo_noalloc_error(int32_t clear, uint32_t* code, void* stream);
 
 /* What kairo_bsr_spmm would run for this problem (no device work).  Fills
  * `out` from the same decision as kairo_bsr_spmm_workspace_size, assuming

@@ -146,6 +146,7 @@ _SIGNATURES = {
                                  c_int32, POINTER(KairoSpmmConfig), c_void_p, c_size_t, c_void_p]),
     "kairo_bsr_spmm_noalloc": (c_int32, [POINTER(KairoBsr), c_void_p, c_int64, c_int32, c_int64, c_void_p,
                                          c_int64, c_int32, POINTER(KairoSpmmConfig), c_void_p]),
+    "kairo_noalloc_error": (c_int32, [c_int32, POINTER(c_uint32), c_void_p]),
     "kairo_bsr_spmm_describe": (c_int32, [POINTER(KairoBsr), c_int32, c_int64, POINTER(KairoSpmmConfig),
                                           POINTER(KairoSpmmPlan)]),
     "kairo_bsr_spmm_workspace_size": (c_int32, [POINTER(KairoBsr), c_int32, c_int64, POINTER(KairoSpmmConfig),
