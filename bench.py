@@ -383,7 +383,8 @@ def run_ours(args) -> None:
     linear = spec.layout == "linear"
     b = problem.b[c0:c1] if linear else problem.b[:, c0:c1]
     cfg = KernelConfig(kernel=args.kernel, n_tile=args.n_tile, group_blocks=args.group_blocks,
-                       schedule=args.schedule, band_rows=args.band_rows, row_cost=args.row_cost)
+                       schedule=args.schedule, band_rows=args.band_rows, row_cost=args.row_cost,
+                       stages=args.stages, num_ctas=args.num_ctas, ctas_per_sm=args.ctas_per_sm)
     plan = describe(a, ncols, linear=linear, config=cfg)
     if linear:
         from kairo_b200.ops import sparse_linear
@@ -524,7 +525,8 @@ def run_ours(args) -> None:
                                 f"of B and C, B replicated)"),
                 "l2": "flushed before every step (256 MiB write, untimed)",
                 "kernel_config": {"kernel": args.kernel, "n_tile": args.n_tile, "group_blocks": args.group_blocks,
-                                  "row_cost": args.row_cost,
+                                  "row_cost": args.row_cost, "stages": args.stages, "num_ctas": args.num_ctas,
+                                  "ctas_per_sm": args.ctas_per_sm,
                                   "schedule": args.schedule, "band_rows": args.band_rows,
                                   "max_row_blocks": a.max_row_blocks},
                 "plan": plan,
@@ -771,7 +773,8 @@ def run_tune(args) -> None:
         except Exception as exc:  # noqa: BLE001 - a variant this shape does not support
             plan = {"unsupported": str(exc)}
         rows.append({"n_tile": kc.n_tile, "stages": kc.stages, "row_cost": kc.row_cost, "schedule": kc.schedule,
-                     "group_blocks": kc.group_blocks, "ms": ms, "tflops": flops(spec) / (ms / 1e3) / 1e12,
+                     "group_blocks": kc.group_blocks, "ctas_per_sm": kc.ctas_per_sm, "ms": ms,
+                     "tflops": flops(spec) / (ms / 1e3) / 1e12,
                      "plan": plan})
     best = tuner.best_kernel_config(a, spec.n)
     print(json.dumps({"op": "tune", "workload": spec.name, "candidates": rows,
@@ -1072,6 +1075,9 @@ def main() -> None:
     ap.add_argument("--schedule", choices=("auto", "rows", "bands"), default="auto")
     ap.add_argument("--band-rows", type=int, default=0)
     ap.add_argument("--row-cost", type=int, default=0, help="scheduler weight of a block-row (0 = library default)")
+    ap.add_argument("--stages", type=int, default=0, help="pipeline stages of the tcgen05 kernel (0 = library default)")
+    ap.add_argument("--num-ctas", type=int, default=0, help="persistent grid size (0 = library default)")
+    ap.add_argument("--ctas-per-sm", type=int, default=0, help="resident CTAs per SM (0 = library default)")
     ap.add_argument("--gather", action="store_true", help="also time the all-gather of C (reported separately)")
     ap.add_argument("--grid", action="store_true",
                     help="at N > 1 arrange the ranks as block-row groups x column slices of B and C "

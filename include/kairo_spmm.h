@@ -122,7 +122,11 @@ typedef struct kairo_spmm_config {
                                 the launch records KAIRO_DEVERR_WAIT_TIMEOUT with the wait's site tag,
                                 drains its copies and MMAs, frees TMEM and returns.  Ignored by the other
                                 kernels. */
-  int32_t reserved[2];
+  int32_t ctas_per_sm;       /* resident CTAs per SM of the row-split tcgen05 kernel, 1..4 (0 = auto):
+                                the SM's shared memory and TMEM are split between them, so that one
+                                CTA's pipeline handoffs overlap another's MMAs; clamped to what the
+                                SM can hold */
+  int32_t reserved[1];
 } kairo_spmm_config;
 
 /* Work schedules of the tcgen05 kernel.

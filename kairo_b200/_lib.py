@@ -95,7 +95,8 @@ class KairoSpmmConfig(Structure):
         ("band_rows", c_int32),
         ("wait_kcycles", c_int32),
         ("debug_hold_stage", c_int32),
-        ("reserved", c_int32 * 2),
+        ("ctas_per_sm", c_int32),
+        ("reserved", c_int32 * 1),
     ]
 
 

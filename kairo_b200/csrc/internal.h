@@ -41,13 +41,25 @@ constexpr size_t kCounterRegionBytes = 2 * kCounterBankEntries * sizeof(unsigned
 // four stages when the B slice of one chunk exceeds half of L2; otherwise
 // three stages of the largest group that fits, or two when fewer than nine
 // block slots fit.
-inline int default_group_blocks(int slots, bool b_slice_exceeds_half_l2) {
-  const int stages = b_slice_exceeds_half_l2 ? 4 : (slots >= 9 ? 3 : 2);
+// With several CTAs per SM the stages of all of them are in flight at once;
+// each CTA then keeps three stages (measured best at two CTAs per SM on the
+// 262144^2, 16384^2 and Zipf workloads).
+inline int default_group_blocks(int slots, bool b_slice_exceeds_half_l2, int ctas_per_sm = 1) {
+  const int stages = ctas_per_sm > 1 ? 3 : (b_slice_exceeds_half_l2 ? 4 : (slots >= 9 ? 3 : 2));
   int g = slots / stages;
   if (g > 32) g = 32;
   if (g < 1) g = 1;
   return g;
 }
+
+// Shared memory of one SM and the part the driver reserves per resident CTA
+// (sm_100: 228 KiB and 1 KiB).
+constexpr int kSmemPerSm = 228 * 1024;
+constexpr int kSmemReservedPerCta = 1024;
+
+// Resident CTAs per SM of the row-split tcgen05 kernel when the caller
+// leaves it to the library.
+int default_ctas_per_sm(const kairo_bsr* a, int nt, int sms);
 
 // Bytes of the B (or X) columns one chunk of 128 * nt output columns reads.
 inline double b_slice_bytes(const kairo_bsr* a, int nt) { return static_cast<double>(a->cols) * 128.0 * nt * 2.0; }
@@ -73,6 +85,7 @@ struct TcPlan {
   size_t workspace_bytes;
   long long wait_cycles;   // bound of every mbarrier wait (kairo_spmm_config.wait_kcycles)
   int hold_stage;          // kairo_spmm_config.debug_hold_stage
+  int ctas_per_sm;         // resident CTAs per SM the shared-memory budget was split for
 };
 
 // TMA tensor maps (tma_maps.cu).  make_operand_maps builds the block-storage

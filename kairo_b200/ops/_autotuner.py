@@ -10,8 +10,8 @@ On B200 the search space gains the Blackwell launch knobs of the tcgen05
 kernel (``BLACKWELL_VARIANTS``): ``n_tile`` (128 or 256 columns of C per work
 item, i.e. one or two M=128 MMAs sharing each block), ``stages``
 (shared-memory pipeline depth), ``row_cost`` (scheduler weight of a
-block-row), ``schedule`` (row split or bands) and ``group_blocks`` (blocks
-per pipeline stage).  They are returned as extra keys.  Candidate tiles are
+block-row), ``schedule`` (row split or bands), ``group_blocks`` (blocks
+per pipeline stage) and ``ctas_per_sm`` (resident CTAs per SM).  They are returned as extra keys.  Candidate tiles are
 built as tile_m x tile_k blocks (the reference times square tile_m tiles
 whatever tile_k is), so each candidate is timed with the kernel it would
 get.  Timing uses CUDA events (median of ``BENCH_ITERS``) instead of host
@@ -49,14 +49,15 @@ class TileConfig:
     row_cost: int = 0
     schedule: str = "auto"
     group_blocks: int = 0
+    ctas_per_sm: int = 0
 
     def __post_init__(self) -> None:
         if min(self.tile_m, self.tile_n, self.tile_k) <= 0:
             raise ValueError("tile sizes must be positive")
         if self.n_tile not in (0, 128, 256):
             raise ValueError("n_tile must be 0, 128 or 256")
-        if self.stages < 0 or self.row_cost < 0 or self.group_blocks < 0:
-            raise ValueError("stages, row_cost and group_blocks must be non-negative")
+        if self.stages < 0 or self.row_cost < 0 or self.group_blocks < 0 or self.ctas_per_sm < 0:
+            raise ValueError("stages, row_cost, group_blocks and ctas_per_sm must be non-negative")
         if self.schedule not in ("auto", "rows", "bands"):
             raise ValueError("schedule must be 'auto', 'rows' or 'bands'")
 
@@ -64,7 +65,7 @@ class TileConfig:
         from kairo_b200.ops.spmm import KernelConfig
 
         return KernelConfig(n_tile=self.n_tile, stages=self.stages, row_cost=self.row_cost,
-                            schedule=self.schedule, group_blocks=self.group_blocks)
+                            schedule=self.schedule, group_blocks=self.group_blocks, ctas_per_sm=self.ctas_per_sm)
 
 
 # Reference candidates (_autotuner.py:25-31), kept for the legacy keys.
@@ -79,17 +80,18 @@ CANDIDATE_CONFIGS: tuple[TileConfig, ...] = (
 DEFAULT_CONFIG = CANDIDATE_CONFIGS[0]
 
 # Blackwell launch variants tried for 16-bit inputs on top of each tile size:
-# (n_tile, stages, row_cost, schedule, group_blocks).
-BLACKWELL_VARIANTS: tuple[tuple[int, int, int, str, int], ...] = (
-    (0, 0, 0, "auto", 0),
-    (128, 0, 0, "auto", 0),
-    (256, 0, 0, "auto", 0),
-    (0, 0, 0, "rows", 0),
-    (0, 0, 0, "bands", 0),
-    (128, 0, 4, "rows", 0),
-    (0, 0, 0, "rows", 2),
-    (0, 0, 0, "rows", 8),
-    (256, 4, 0, "rows", 0),
+# (n_tile, stages, row_cost, schedule, group_blocks, ctas_per_sm).
+BLACKWELL_VARIANTS: tuple[tuple[int, int, int, str, int, int], ...] = (
+    (0, 0, 0, "auto", 0, 0),
+    (128, 0, 0, "auto", 0, 0),
+    (256, 0, 0, "auto", 0, 0),
+    (0, 0, 0, "rows", 0, 1),
+    (0, 0, 0, "rows", 0, 2),
+    (0, 0, 0, "bands", 0, 0),
+    (128, 0, 4, "rows", 0, 0),
+    (0, 0, 0, "rows", 2, 2),
+    (0, 0, 0, "rows", 8, 1),
+    (256, 4, 0, "rows", 0, 1),
 )
 
 BENCH_WARMUP = 2
@@ -162,9 +164,10 @@ class TileAutotuner:
             if cfg.tile_m > M or cfg.tile_k > K:
                 continue
             square16 = dtype in (torch.float16, torch.bfloat16) and cfg.tile_m == cfg.tile_k
-            variants = BLACKWELL_VARIANTS if square16 else ((0, 0, 0, "auto", 0),)
-            for n_tile, stages, row_cost, schedule, group in variants:
-                out.append(TileConfig(cfg.tile_m, cfg.tile_n, cfg.tile_k, n_tile, stages, row_cost, schedule, group))
+            variants = BLACKWELL_VARIANTS if square16 else ((0, 0, 0, "auto", 0, 0),)
+            for n_tile, stages, row_cost, schedule, group, per_sm in variants:
+                out.append(TileConfig(cfg.tile_m, cfg.tile_n, cfg.tile_k, n_tile, stages, row_cost, schedule, group,
+                                      per_sm))
         return out
 
     def _benchmark(self, M: int, K: int, N: int, sparsity: float, dtype: torch.dtype,
@@ -211,8 +214,9 @@ class TileAutotuner:
         from kairo_b200.ops.spmm import KernelConfig, block_sparse_mm_bsr
 
         if candidates is None:
-            candidates = [KernelConfig(n_tile=nt, stages=st, row_cost=rc, schedule=sc, group_blocks=gb)
-                          for nt, st, rc, sc, gb in BLACKWELL_VARIANTS]
+            candidates = [KernelConfig(n_tile=nt, stages=st, row_cost=rc, schedule=sc, group_blocks=gb,
+                                       ctas_per_sm=per_sm)
+                          for nt, st, rc, sc, gb, per_sm in BLACKWELL_VARIANTS]
         if B is None:
             B = torch.randn(a.shape[1], N, device=a.device).to(a.dtype)
         out = torch.empty(a.shape[0], N, dtype=torch.float32, device=a.device)
@@ -241,7 +245,8 @@ class TileAutotuner:
                 best, best_t = kc, t
         self._cache[key] = {"kernel": best.kernel, "n_tile": best.n_tile, "stages": best.stages,
                             "row_cost": best.row_cost, "num_ctas": best.num_ctas, "schedule": best.schedule,
-                            "group_blocks": best.group_blocks, "band_rows": best.band_rows}
+                            "group_blocks": best.group_blocks, "band_rows": best.band_rows,
+                            "ctas_per_sm": best.ctas_per_sm}
         return best
 
     def clear_cache(self) -> None:
@@ -282,4 +287,5 @@ def _config_to_dict(cfg: TileConfig) -> dict[str, Any]:
         "row_cost": cfg.row_cost,
         "schedule": cfg.schedule,
         "group_blocks": cfg.group_blocks,
+        "ctas_per_sm": cfg.ctas_per_sm,
     }

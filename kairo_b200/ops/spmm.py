@@ -36,7 +36,9 @@ class KernelConfig:
     nonzero blocks loaded per pipeline stage (1..32); schedule: "auto",
     "rows" (block-rows split over CTAs, robust to skew) or "bands" (CTAs
     sweep B panels together, for a B slice larger than L2); band_rows:
-    block-rows per band item.  Debugging knobs: wait_kcycles bounds every
+    block-rows per band item; ctas_per_sm: resident CTAs per SM of the
+    row-split kernel (1..4), which share the SM's shared memory and TMEM so
+    that one CTA's pipeline handoffs overlap another's MMAs.  Debugging knobs: wait_kcycles bounds every
     pipeline wait of the tcgen05 kernels (thousands of SM cycles; 0 = the
     default of about 4 s); debug_hold_stage=1 (a test hook) makes the
     row-split kernel hold back its first stage so that a bounded wait runs
@@ -53,6 +55,7 @@ class KernelConfig:
     band_rows: int = 0
     wait_kcycles: int = 0
     debug_hold_stage: int = 0
+    ctas_per_sm: int = 0
 
     def __post_init__(self) -> None:
         if self.kernel not in ("auto", "simt", "tcgen05", "split_bf16"):
@@ -63,7 +66,9 @@ class KernelConfig:
             raise ValueError(f"schedule must be 'auto', 'rows' or 'bands', got {self.schedule!r}")
         if self.debug_hold_stage not in (0, 1):
             raise ValueError("debug_hold_stage must be 0 or 1")
-        for name in ("stages", "row_cost", "num_ctas", "group_blocks", "band_rows", "wait_kcycles"):
+        if self.ctas_per_sm > 4:
+            raise ValueError("ctas_per_sm must be at most 4")
+        for name in ("stages", "row_cost", "num_ctas", "group_blocks", "band_rows", "wait_kcycles", "ctas_per_sm"):
             if getattr(self, name) < 0:
                 raise ValueError(f"{name} must be non-negative")
         if self.group_blocks > 32:
@@ -82,6 +87,7 @@ class KernelConfig:
         c.band_rows = self.band_rows
         c.wait_kcycles = self.wait_kcycles
         c.debug_hold_stage = self.debug_hold_stage
+        c.ctas_per_sm = self.ctas_per_sm
         return c
 
 

@@ -34,7 +34,7 @@ def test_best_config_times_on_the_gpu_and_its_choice_matches_the_oracle(dtype):
     p = generate(spec, seed=8)
     a = bsr_from_tiles(p.tiles.cuda(), p.row_ids.cuda(), p.col_ids.cuda(), (M, K))
     kc = KernelConfig(n_tile=cfg["n_tile"], stages=cfg["stages"], row_cost=cfg["row_cost"],
-                      schedule=cfg["schedule"], group_blocks=cfg["group_blocks"])
+                      schedule=cfg["schedule"], group_blocks=cfg["group_blocks"], ctas_per_sm=cfg["ctas_per_sm"])
     c = block_sparse_mm_bsr(a, p.b.cuda(), config=kc, check=True)
     ref = oracle.spmm_tiles(p.tiles, p.row_ids, p.col_ids, p.b, M, K, N, spec.block)
     assert rel_fro(c, ref) <= TOL

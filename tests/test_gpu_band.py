@@ -153,8 +153,11 @@ def test_schedule_choice():
     assert describe(a, 1024)["schedule"] == "rows"
     assert describe(a, 1024, config=KernelConfig(schedule="bands"))["schedule"] == "bands"
     plan = describe(a, 1024)
-    # B slice above half of L2: four pipeline stages of three 18 KB slots
-    assert (plan["stages"], plan["group_blocks"]) == (4, 3)
+    # 32x32 blocks: two CTAs per SM, each with three stages of two 18 KB slots
+    assert plan["grid"] == 2 * sms and (plan["stages"], plan["group_blocks"]) == (3, 2)
+    # one CTA per SM with the B slice above half of L2: four stages of three slots
+    one = describe(a, 1024, config=KernelConfig(ctas_per_sm=1))
+    assert one["grid"] == sms and (one["stages"], one["group_blocks"]) == (4, 3)
     # few long rows, many chunks (the linear layer): bands
     few = max(1, sms // 2)
     b = _uniform_rows_matrix(few, 512, 100, 64, max_row_blocks=100)
@@ -163,8 +166,9 @@ def test_schedule_choice():
     assert describe(_uniform_rows_matrix(few, 512, 100, 64, max_row_blocks=0), 8192)["schedule"] == "rows"
     assert describe(_uniform_rows_matrix(few, 512, 100, 64, max_row_blocks=400), 8192)["schedule"] == "rows"
     a2 = _uniform_rows_matrix(1024, 512, 41, 32, max_row_blocks=41)
-    plan2 = describe(a2, 1024)
+    plan2 = describe(a2, 1024, config=KernelConfig(ctas_per_sm=1))
     assert plan2["schedule"] == "rows" and (plan2["stages"], plan2["group_blocks"]) == (3, 4)
+    assert (describe(a2, 1024)["stages"], describe(a2, 1024)["group_blocks"]) == (3, 2)
     # many rows on a dense block grid (the transposed linear-layer weight,
     # 20 % of 512 x 128 blocks): bands
     c = _uniform_rows_matrix(512, 128, 26, 64, max_row_blocks=26)
