@@ -459,24 +459,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (it.kind == kPartial)
         part = args.partials + (static_cast<int64_t>(it.group * G + blockIdx.x) * 2 + it.slot) * PART_ELEMS;
       const uint32_t slot_cols = static_cast<uint32_t>(slot * ACC_COLS);
+      if constexpr (ACC_COLS <= 64) {
+        // The whole accumulator (up to 64 values per thread) is loaded with
+        // back-to-back TMEM loads and one wait, and its slot is released
+        // before the stores to C, so the MMA warp can reuse it while they
+        // drain.  With short block-rows the epilogue is otherwise what the
+        // MMA warp waits for.
+        float v[ACC_COLS];
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
+        for (int t = 0; t < NT; ++t)
 #pragma unroll
-        for (int j0 = 0; j0 < BM; j0 += 16) {
-          float v[16];
-          ptx::tmem_ld16(tmem_base + lane_addr + slot_cols + static_cast<uint32_t>(t * BM + j0), v);
-          ptx::tmem_wait_ld();
-          if (it.kind == kDirect) {
-            store16<LINEAR, TOut>(args, it.row, BM, j0, n0 + t * 128 + e, v);
-          } else {
+          for (int j0 = 0; j0 < BM; j0 += 16)
+            ptx::tmem_ld16(tmem_base + lane_addr + slot_cols + static_cast<uint32_t>(t * BM + j0), v + t * BM + j0);
+        ptx::tmem_wait_ld();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&tempty[slot]);
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) part[(t * BM + j0 + jj) * 128 + e] = v[jj];
+        for (int t = 0; t < NT; ++t) {
+#pragma unroll
+          for (int j0 = 0; j0 < BM; j0 += 16) {
+            if (it.kind == kDirect) {
+              store16<LINEAR, TOut>(args, it.row, BM, j0, n0 + t * 128 + e, v + t * BM + j0);
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) part[(t * BM + j0 + jj) * 128 + e] = v[t * BM + j0 + jj];
+            }
           }
         }
+      } else {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+#pragma unroll
+          for (int j0 = 0; j0 < BM; j0 += 16) {
+            float v[16];
+            ptx::tmem_ld16(tmem_base + lane_addr + slot_cols + static_cast<uint32_t>(t * BM + j0), v);
+            ptx::tmem_wait_ld();
+            if (it.kind == kDirect) {
+              store16<LINEAR, TOut>(args, it.row, BM, j0, n0 + t * 128 + e, v);
+            } else {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) part[(t * BM + j0 + jj) * 128 + e] = v[jj];
+            }
+          }
+        }
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&tempty[slot]);
       }
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&tempty[slot]);
       slot ^= 1;
       if (slot == 0) aphase ^= 1u;
       if (it.kind == kPartial) {
