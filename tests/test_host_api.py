@@ -218,3 +218,32 @@ def test_accounting_matches_definitions():
     assert WORKLOADS["fp16_zipf"].nnzb == 167772
     assert WORKLOADS["bf16_linear"].nnzb == 13107
     assert WORKLOADS["fp32_uniform"].nnzb == 6553
+
+
+def test_new_launch_knobs_are_validated_and_reach_the_c_struct():
+    from kairo_b200.ops import KernelConfig
+
+    c = KernelConfig(ctas_per_sm=2, wait_kcycles=500, debug_hold_stage=1).to_c()
+    assert (c.ctas_per_sm, c.wait_kcycles, c.debug_hold_stage) == (2, 500, 1)
+    with pytest.raises(ValueError):
+        KernelConfig(ctas_per_sm=5)
+    with pytest.raises(ValueError):
+        KernelConfig(debug_hold_stage=2)
+    with pytest.raises(ValueError):
+        KernelConfig(wait_kcycles=-1)
+
+
+def test_autotuner_candidates_and_key():
+    import torch as _t
+    from kairo_b200.ops._autotuner import BLACKWELL_VARIANTS, CANDIDATE_CONFIGS, TileAutotuner, _cache_key
+
+    tuner = TileAutotuner()
+    square = [c for c in CANDIDATE_CONFIGS if c.tile_m == c.tile_k]
+    cands = tuner.candidates(1024, 1024, _t.bfloat16)
+    assert len(cands) == len(square) * len(BLACKWELL_VARIANTS) + len(CANDIDATE_CONFIGS) - len(square)
+    assert all(c.tile_m == c.tile_k or (c.n_tile, c.schedule, c.ctas_per_sm) == (0, "auto", 0) for c in cands)
+    assert len(tuner.candidates(1024, 1024, _t.float32)) == len(CANDIDATE_CONFIGS)
+    assert {c.tile_m for c in tuner.candidates(1024, 1024, _t.float16, block=32)} == {32}
+    # the reference's 4-argument key is unchanged; dtype and block are appended
+    assert _cache_key(256, 256, 128, 0.5) == "512_512_128_0.5"
+    assert _cache_key(256, 256, 128, 0.5, _t.bfloat16, 32) == "512_512_128_0.5_bfloat16_b32"
