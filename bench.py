@@ -3,9 +3,10 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload NAME] [--gather]
 
-One process per GPU (torchrun for N > 1).  A is sharded by nnz-balanced
-block-row ranges, B is replicated, and no collective runs on the compute path.
-Every rank generates the same seeded workload on its device and keeps its own
+One process per GPU (torchrun for N > 1).  The ranks form a grid of
+nnz-balanced block-row groups x column slices of B and C (``--rows``: block-row
+ranges only, B replicated); no collective runs on the compute path.  Every
+rank generates the same seeded workload on its device and keeps its own
 shard.  A step is one SpMM launch over the local shard.  It is timed with CUDA
 events on the launching stream.  The L2 is flushed before every step by
 writing a 256 MiB buffer, which is not timed.  The job's time is the max over
@@ -366,12 +367,14 @@ def run_ours(args) -> None:
     t0 = time.perf_counter()
     problem = generate(spec, seed=args.seed, device=dev)
     a_full = bsr_from_tiles(problem.tiles, problem.row_ids, problem.col_ids, (spec.m, spec.k))
-    # Default: the configuration's decomposition, nnz-balanced block-row
-    # ranges with B replicated.  --grid: ranks form a (row groups x column
-    # slices) grid, C's columns (the batch rows of X in the linear layout)
-    # sliced as well.  No collective on the compute path either way.
+    # Default: the ranks form a (row groups x column slices) grid: within
+    # its row group a rank takes an nnz-balanced block-row range, and its
+    # column slice is a range of C's (and B's) columns (the batch rows of X
+    # in the linear layout); grid_shape picks the shape (2 x 1, 2 x 2, 4 x 2
+    # at 2, 4, 8 GPUs for the 262144^2 case).  --rows: block-row ranges
+    # only, B replicated.  No collective on the compute path either way.
     row_group, col_slice, row_groups, col_slices = rank, 0, world, 1
-    if args.grid:
+    if not args.rows:
         row_group, col_slice, row_groups, col_slices = grid_coords(rank, world, spec.n, 256,
                                                                    *operand_bytes(a_full, spec.n))
     bounds = partition_rows(a_full.row_ptr, row_groups)
@@ -522,7 +525,7 @@ def run_ours(args) -> None:
                 "workload": spec.name, "m": spec.m, "k": spec.k, "n": spec.n, "block": spec.block,
                 "sparsity": spec.sparsity, "nnzb": a_full.nnzb, "out_dtype": str(spec.out_dtype).replace("torch.", ""),
                 "parallelism": (f"grid {row_groups}x{col_slices} (nnz-balanced block-row groups x column slices "
-                                f"of B and C, B replicated)"),
+                                f"of B and C; each column slice of B replicated over the row groups)"),
                 "l2": "flushed before every step (256 MiB write, untimed)",
                 "kernel_config": {"kernel": args.kernel, "n_tile": args.n_tile, "group_blocks": args.group_blocks,
                                   "row_cost": args.row_cost, "stages": args.stages, "num_ctas": args.num_ctas,
@@ -1079,9 +1082,9 @@ def main() -> None:
     ap.add_argument("--num-ctas", type=int, default=0, help="persistent grid size (0 = library default)")
     ap.add_argument("--ctas-per-sm", type=int, default=0, help="resident CTAs per SM (0 = library default)")
     ap.add_argument("--gather", action="store_true", help="also time the all-gather of C (reported separately)")
-    ap.add_argument("--grid", action="store_true",
-                    help="at N > 1 arrange the ranks as block-row groups x column slices of B and C "
-                         "(default: block-row ranges only, B replicated)")
+    ap.add_argument("--rows", action="store_true",
+                    help="at N > 1 split A into nnz-balanced block-row ranges only, B replicated "
+                         "(default: a grid of block-row groups x column slices of B and C)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true")
