@@ -690,7 +690,7 @@ def run_backward(args) -> None:
     wt = bsr_transpose(w, check=True)
     dx = torch.empty(spec.n, spec.k, dtype=spec.dtype, device=dev)
     cfg = KernelConfig(n_tile=args.n_tile, group_blocks=args.group_blocks, schedule=args.schedule,
-                       band_rows=args.band_rows)
+                       band_rows=args.band_rows, ctas_per_sm=args.ctas_per_sm)
     parts = ("wt_values", "dx", "dw")
 
     def part(name):

@@ -122,10 +122,10 @@ typedef struct kairo_spmm_config {
                                 the launch records KAIRO_DEVERR_WAIT_TIMEOUT with the wait's site tag,
                                 drains its copies and MMAs, frees TMEM and returns.  Ignored by the other
                                 kernels. */
-  int32_t ctas_per_sm;       /* resident CTAs per SM of the row-split tcgen05 kernel, 1..4 (0 = auto):
-                                the SM's shared memory and TMEM are split between them, so that one
-                                CTA's pipeline handoffs overlap another's MMAs; clamped to what the
-                                SM can hold */
+  int32_t ctas_per_sm;       /* resident CTAs per SM of the tcgen05 kernels, 1..4 (0 = auto: 2, or 1 for
+                                the row-split schedule with 64-row blocks): the SM's shared memory and
+                                TMEM are split between them, so that one CTA's pipeline handoffs
+                                overlap another's MMAs; clamped to what the SM can hold */
   int32_t reserved[1];
 } kairo_spmm_config;
 

@@ -88,6 +88,7 @@ BLACKWELL_VARIANTS: tuple[tuple[int, int, int, str, int, int], ...] = (
     (0, 0, 0, "rows", 0, 1),
     (0, 0, 0, "rows", 0, 2),
     (0, 0, 0, "bands", 0, 0),
+    (0, 0, 0, "bands", 0, 1),
     (128, 0, 4, "rows", 0, 0),
     (0, 0, 0, "rows", 2, 2),
     (0, 0, 0, "rows", 8, 1),

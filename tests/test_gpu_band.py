@@ -162,6 +162,12 @@ def test_schedule_choice():
     few = max(1, sms // 2)
     b = _uniform_rows_matrix(few, 512, 100, 64, max_row_blocks=100)
     assert describe(b, 8192)["schedule"] == "bands"
+    # two CTAs per SM by default, each with one 64-row block-row per item
+    assert describe(b, 8192)["grid"] == 2 * sms
+    assert describe(b, 8192, config=KernelConfig(ctas_per_sm=1))["grid"] == sms
+    # ... and one when the caller's band_rows need the whole TMEM
+    wide = describe(b, 8192, config=KernelConfig(band_rows=4))
+    assert wide["grid"] == sms and wide["rows"] == 4
     # ... but not without the row-length hint, nor with a very long row
     assert describe(_uniform_rows_matrix(few, 512, 100, 64, max_row_blocks=0), 8192)["schedule"] == "rows"
     assert describe(_uniform_rows_matrix(few, 512, 100, 64, max_row_blocks=400), 8192)["schedule"] == "rows"
@@ -181,3 +187,22 @@ def test_build_reports_longest_row():
     a = bsr_from_tiles(p.tiles.to(DEV), p.row_ids.to(DEV), p.col_ids.to(DEV), (2048, 2048))
     counts = torch.bincount(p.row_ids.long(), minlength=a.nbr)
     assert a.max_row_blocks == int(counts.max())
+
+
+@pytest.mark.parametrize("per_sm", [1, 2])
+@pytest.mark.parametrize("shape", [(512, 2048, 1024, 64, 0.8), (1024, 1024, 512, 32, 0.7)])
+def test_band_ctas_per_sm_vs_oracle(shape, per_sm):
+    """The band schedule with one and with two resident CTAs per SM (two
+    split the TMEM and shared memory: one block-row per item for 64x64
+    blocks)."""
+    m, k, n, bs, sp = shape
+    spec = WorkloadSpec("t", torch.bfloat16, m, k, n, bs, sp)
+    p = generate(spec, seed=12)
+    a = bsr_from_tiles(p.tiles.to(DEV), p.row_ids.to(DEV), p.col_ids.to(DEV), (m, k))
+    cfg = KernelConfig(schedule="bands", ctas_per_sm=per_sm)
+    plan = describe(a, n, config=cfg)
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert plan["schedule"] == "bands" and plan["grid"] <= per_sm * sms
+    c = block_sparse_mm_bsr(a, p.b.to(DEV), config=cfg, check=True)
+    ref = oracle.spmm_tiles(p.tiles, p.row_ids, p.col_ids, p.b, m, k, n, bs)
+    assert rel_fro(c, ref) <= TOL
