@@ -387,8 +387,11 @@ def run_ours(args) -> None:
     b = problem.b[c0:c1] if linear else problem.b[:, c0:c1]
     cfg = KernelConfig(kernel=args.kernel, n_tile=args.n_tile, group_blocks=args.group_blocks,
                        schedule=args.schedule, band_rows=args.band_rows, row_cost=args.row_cost,
-                       stages=args.stages, num_ctas=args.num_ctas, ctas_per_sm=args.ctas_per_sm)
-    plan = describe(a, ncols, linear=linear, config=cfg)
+                       stages=args.stages, num_ctas=args.num_ctas, ctas_per_sm=args.ctas_per_sm,
+                       group_rows=args.group_rows)
+    t_groups = time.perf_counter()
+    plan = describe(a, ncols, linear=linear, config=cfg)  # builds (and caches) row groups when they are used
+    groups_build_s = time.perf_counter() - t_groups
     if linear:
         from kairo_b200.ops import sparse_linear
 
@@ -531,8 +534,9 @@ def run_ours(args) -> None:
                                   "row_cost": args.row_cost, "stages": args.stages, "num_ctas": args.num_ctas,
                                   "ctas_per_sm": args.ctas_per_sm,
                                   "schedule": args.schedule, "band_rows": args.band_rows,
-                                  "max_row_blocks": a.max_row_blocks},
+                                  "group_rows": args.group_rows, "max_row_blocks": a.max_row_blocks},
                 "plan": plan,
+                **({"row_groups_build_ms": round(groups_build_s * 1e3, 3)} if plan["schedule"] == "groups" else {}),
             },
             "roofline": {
                 **roof,
@@ -1075,7 +1079,8 @@ def main() -> None:
                     help="kernel family (split_bf16: fp32 workloads on the tensor cores, opt-in)")
     ap.add_argument("--n-tile", type=int, default=0)
     ap.add_argument("--group-blocks", type=int, default=0)
-    ap.add_argument("--schedule", choices=("auto", "rows", "bands"), default="auto")
+    ap.add_argument("--schedule", choices=("auto", "rows", "bands", "groups"), default="auto")
+    ap.add_argument("--group-rows", type=int, default=0, help="block-rows per row group (2, 4, 8; 0 = 4)")
     ap.add_argument("--band-rows", type=int, default=0)
     ap.add_argument("--row-cost", type=int, default=0, help="scheduler weight of a block-row (0 = library default)")
     ap.add_argument("--stages", type=int, default=0, help="pipeline stages of the tcgen05 kernel (0 = library default)")

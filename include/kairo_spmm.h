@@ -143,7 +143,8 @@ typedef struct kairo_spmm_config {
 typedef enum kairo_schedule {
   KAIRO_SCHEDULE_AUTO = 0,
   KAIRO_SCHEDULE_ROWS = 1,
-  KAIRO_SCHEDULE_BANDS = 2
+  KAIRO_SCHEDULE_BANDS = 2,
+  KAIRO_SCHEDULE_GROUPS = 3  /* row groups (kairo_bsr_spmm_stacked); reported by describe, not a selector here */
 } kairo_schedule;
 
 /* Operand layouts of kairo_bsr_spmm. */
@@ -210,6 +211,56 @@ KAIRO_API kairo_status kairo_bsr_spmm_describe(const kairo_bsr* a, int32_t layou
 /* Bytes of zero-initialised workspace kairo_bsr_spmm needs for this problem. */
 KAIRO_API kairo_status kairo_bsr_spmm_workspace_size(const kairo_bsr* a, int32_t layout, int64_t n,
                                            const kairo_spmm_config* cfg, size_t* bytes);
+
+/* ------------------------------------------------------------------------
+ * Row groups: the same SpMM for masks whose block-rows are long and share
+ * columns (a skewed mask such as Zipf row counts, where a few rows hold most
+ * blocks).  The block-rows, ordered by block count (longest first, ties by
+ * index), are taken R at a time; a group's "stacked blocks" are its distinct
+ * column-blocks, each with a mask of the group rows that have a block there.
+ * The tcgen05 kernel then loads one B panel per stacked block and multiplies
+ * each run of consecutive present rows with one MMA of N = run * bm.  Same
+ * result as kairo_bsr_spmm (fp32 accumulate; the sums run in another order,
+ * so the two agree to fp32 rounding, not bit for bit).  No counterpart in
+ * the reference: the reference has one kernel for every mask
+ * (csrc/acc_spmm_kernel.cu:158-207); this is an added schedule for the
+ * operator that kairo/ops/spmm.py:58-105 defines.
+ *
+ * kairo_bsr_stack_build builds the groups on the device into `mem`
+ * (kairo_bsr_stack_size bytes), fills `out` and synchronises `stream` once
+ * (it reads the stacked-block count back).  R is 2, 4 or 8; nbr and the
+ * number of block-columns must be at most 16384.  A block-row holding two
+ * blocks in one column returns NOT_SUPPORTED; a column index out of range
+ * returns INVALID_VALUE.  The structure depends only on row_ptr / col_idx /
+ * blk_idx: it stays valid while those are unchanged (block values may
+ * change).
+ * kairo_bsr_spmm_stacked: STANDARD layout, f16/bf16 square blocks of 16 or
+ * 32, fp32 C; R * bm * (n_tile / 128) must be at most 128 (n_tile 256 is
+ * used when N > 128 and that product allows it).
+ * ---------------------------------------------------------------------- */
+typedef struct kairo_bsr_stack {
+  int32_t rows_per_group;    /* R */
+  int32_t ngroups;           /* ceil(nbr / R) */
+  int64_t nsuper;            /* stacked blocks */
+  const int32_t* group_ptr;  /* ngroups + 1: stacked blocks of each group */
+  const int32_t* super_col;  /* nsuper: column-block of each stacked block, ascending within a group */
+  const int32_t* super_mask; /* nsuper: bit r set when group row r has a block in that column */
+  const int32_t* super_blk;  /* nsuper * R: stored-block index (blk_idx) of each present block */
+  const int32_t* row_map;    /* ngroups * R: block-row of each group row, -1 past the last */
+} kairo_bsr_stack;
+
+KAIRO_API kairo_status kairo_bsr_stack_size(const kairo_bsr* a, int32_t rows_per_group, size_t* bytes);
+KAIRO_API kairo_status kairo_bsr_stack_build(const kairo_bsr* a, int32_t rows_per_group, void* mem,
+                                             size_t mem_bytes, kairo_bsr_stack* out, void* stream);
+KAIRO_API kairo_status kairo_bsr_spmm_stacked_workspace_size(const kairo_bsr* a, const kairo_bsr_stack* s,
+                                                             int64_t n, const kairo_spmm_config* cfg,
+                                                             size_t* bytes);
+KAIRO_API kairo_status kairo_bsr_spmm_stacked_describe(const kairo_bsr* a, const kairo_bsr_stack* s, int64_t n,
+                                                       const kairo_spmm_config* cfg, kairo_spmm_plan* out);
+KAIRO_API kairo_status kairo_bsr_spmm_stacked(const kairo_bsr* a, const kairo_bsr_stack* s, const void* b,
+                                              int64_t ldb, int64_t n, void* c, int64_t ldc,
+                                              const kairo_spmm_config* cfg, void* workspace,
+                                              size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
  * COO tile list -> BSR, on the device, bit-identical to the reference's

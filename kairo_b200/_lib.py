@@ -45,6 +45,7 @@ LAYOUT_LINEAR = 1
 SCHEDULE_AUTO = 0
 SCHEDULE_ROWS = 1
 SCHEDULE_BANDS = 2
+SCHEDULE_GROUPS = 3
 
 ABI_VERSION = 2
 
@@ -114,6 +115,21 @@ class KairoSpmmPlan(Structure):
     ]
 
 
+class KairoBsrStack(Structure):
+    """kairo_bsr_stack: row groups of a BSR matrix (kairo_bsr_stack_build)."""
+
+    _fields_ = [
+        ("rows_per_group", c_int32),
+        ("ngroups", c_int32),
+        ("nsuper", c_int64),
+        ("group_ptr", c_void_p),
+        ("super_col", c_void_p),
+        ("super_mask", c_void_p),
+        ("super_blk", c_void_p),
+        ("row_map", c_void_p),
+    ]
+
+
 class KairoLibraryError(RuntimeError):
     """The native library is missing, failed to build, or failed to load."""
 
@@ -152,6 +168,16 @@ _SIGNATURES = {
                                           POINTER(KairoSpmmPlan)]),
     "kairo_bsr_spmm_workspace_size": (c_int32, [POINTER(KairoBsr), c_int32, c_int64, POINTER(KairoSpmmConfig),
                                                 POINTER(c_size_t)]),
+    "kairo_bsr_stack_size": (c_int32, [POINTER(KairoBsr), c_int32, POINTER(c_size_t)]),
+    "kairo_bsr_stack_build": (c_int32, [POINTER(KairoBsr), c_int32, c_void_p, c_size_t, POINTER(KairoBsrStack),
+                                        c_void_p]),
+    "kairo_bsr_spmm_stacked_workspace_size": (c_int32, [POINTER(KairoBsr), POINTER(KairoBsrStack), c_int64,
+                                                        POINTER(KairoSpmmConfig), POINTER(c_size_t)]),
+    "kairo_bsr_spmm_stacked_describe": (c_int32, [POINTER(KairoBsr), POINTER(KairoBsrStack), c_int64,
+                                                  POINTER(KairoSpmmConfig), POINTER(KairoSpmmPlan)]),
+    "kairo_bsr_spmm_stacked": (c_int32, [POINTER(KairoBsr), POINTER(KairoBsrStack), c_void_p, c_int64, c_int64,
+                                         c_void_p, c_int64, POINTER(KairoSpmmConfig), c_void_p, c_size_t,
+                                         c_void_p]),
     "kairo_bsr_build": (c_int32, [c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p, c_void_p, c_void_p,
                                   POINTER(c_int32), POINTER(c_int32), c_void_p, c_size_t, c_void_p]),
     "kairo_bsr_build_workspace_size": (c_int32, [c_int64, c_int32, POINTER(c_size_t)]),

@@ -86,6 +86,7 @@ struct TcPlan {
   long long wait_cycles;   // bound of every mbarrier wait (kairo_spmm_config.wait_kcycles)
   int hold_stage;          // kairo_spmm_config.debug_hold_stage
   int ctas_per_sm;         // resident CTAs per SM the shared-memory budget was split for
+  int rg;                  // block-rows per item (1, or the row-group size)
 };
 
 // TMA tensor maps (tma_maps.cu).  make_operand_maps builds the block-storage
@@ -96,6 +97,9 @@ kairo_status make_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType
                          uint32_t box_outer, const char* what);
 kairo_status make_map_b3d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t n, uint64_t k,
                           uint64_t ldb, uint32_t bk, uint32_t atoms);
+// The block storage as runs of `blocks` consecutive blocks (one box of
+// blocks * bm rows, at most 256), for copying a stage of consecutive blocks.
+kairo_status make_block_run_map(const kairo_bsr* a, int blocks, CUtensorMap* map);
 kairo_status make_operand_maps(const kairo_bsr* a, const void* b, int64_t ldb, bool linear, int64_t n, int nt,
                                CUtensorMap* map_a, CUtensorMap* map_b, int* b_box3d);
 
@@ -133,8 +137,14 @@ kairo_status band_launch(const kairo_bsr* a, const void* b, int64_t ldb, int32_t
 // tcgen05 path (spmm_tc.cu)
 bool tc_supported(const kairo_bsr* a, int32_t layout, int64_t n, int64_t ldb, int64_t ldc,
                   kairo_dtype c_dtype, const void* b, const void* c, std::string* why);
+// rg > 1 plans a row-group launch: `a` then describes the groups (nbr =
+// groups, nnzb = stacked blocks), and slots, accumulators and partial tiles
+// hold rg blocks' rows.
 kairo_status tc_plan(const kairo_bsr* a, int32_t layout, int64_t n, const kairo_spmm_config* cfg,
-                     int device, TcPlan* plan);
+                     int device, TcPlan* plan, int rg = 1);
+// Counter bank (0 or 1) of the next row-split launch on `workspace`; the
+// banks alternate per workspace (spmm_tc.cu).
+int tc_next_counter_bank(void* workspace);
 kairo_status tc_launch(const kairo_bsr* a, const void* b, int64_t ldb, int32_t layout, int64_t n,
                        void* c, int64_t ldc, kairo_dtype c_dtype, const TcPlan& plan,
                        void* workspace, cudaStream_t stream);

@@ -33,9 +33,18 @@ inline long long wait_bound_cycles(const kairo_spmm_config* cfg) {
 }
 
 // Bytes of one pipeline slot: the B panel (NT sub-tiles of 128 x bk) and the
-// block (bm x bk), the block padded to 1 KiB for its swizzle atom.
-constexpr int stage_bytes(int bm, int bk, int nt) {
-  return nt * 128 * bk * 2 + (bm * bk * 2 + 1023) / 1024 * 1024;
+// block (bm x bk; rg blocks side by side for row groups), padded to 1 KiB for
+// the swizzle atom.
+constexpr int stage_bytes(int bm, int bk, int nt, int rg = 1) {
+  return nt * 128 * bk * 2 + (rg * bm * bk * 2 + 1023) / 1024 * 1024;
+}
+
+// Bytes of one stage of `group` blocks of the row-split tcgen05 kernel:
+// rg = 1: the group's B panels, then its blocks packed, rounded up to 1 KiB;
+// rg > 1: `group` slots of one panel and rg blocks (stage_bytes each).
+__host__ __device__ constexpr int tc_stage_bytes(int bm, int bk, int nt, int rg, int group) {
+  return rg == 1 ? (group * (nt * 128 * bk * 2 + bm * bk * 2) + 1023) / 1024 * 1024
+                 : group * (nt * 128 * bk * 2 + (rg * bm * bk * 2 + 1023) / 1024 * 1024);
 }
 
 template <typename TOut>

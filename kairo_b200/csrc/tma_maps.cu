@@ -76,6 +76,14 @@ kairo_status make_map_b3d(CUtensorMap* map, const void* base, CUtensorMapDataTyp
   return KAIRO_STATUS_SUCCESS;
 }
 
+kairo_status make_block_run_map(const kairo_bsr* a, int blocks, CUtensorMap* map) {
+  const CUtensorMapDataType dt =
+      a->dtype == KAIRO_DTYPE_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  return make_map_2d(map, a->blocks, dt, 2, static_cast<uint64_t>(a->bk),
+                     static_cast<uint64_t>(a->nblocks_stored) * a->bm, static_cast<uint64_t>(a->bk),
+                     static_cast<uint32_t>(a->bk), static_cast<uint32_t>(blocks * a->bm), "runs of block storage");
+}
+
 kairo_status make_operand_maps(const kairo_bsr* a, const void* b, int64_t ldb, bool linear, int64_t n, int nt,
                                CUtensorMap* map_a, CUtensorMap* map_b, int* b_box3d) {
   const CUtensorMapDataType dt =

@@ -20,10 +20,12 @@ from kairo_b200.ops.backward import (
 )
 from kairo_b200.ops.spmm import (
     KernelConfig,
+    RowGroups,
     block_sparse_mm,
     block_sparse_mm_bsr,
     bsr_from_mask,
     bsr_from_tiles,
+    bsr_row_groups,
     describe,
     pending_device_error,
     sparse_linear,
@@ -46,6 +48,8 @@ __all__ = [
     "block_sparse_mm_bsr",
     "bsr_from_mask",
     "bsr_from_tiles",
+    "bsr_row_groups",
+    "RowGroups",
     "describe",
     "pending_device_error",
     "sparse_linear",

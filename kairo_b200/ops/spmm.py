@@ -35,8 +35,11 @@ class KernelConfig:
     (row-split schedule); num_ctas: persistent grid size; group_blocks:
     nonzero blocks loaded per pipeline stage (1..32); schedule: "auto",
     "rows" (block-rows split over CTAs, robust to skew) or "bands" (CTAs
-    sweep B panels together, for a B slice larger than L2); band_rows:
-    block-rows per band item; ctas_per_sm: resident CTAs per SM of the
+    sweep B panels together, for a B slice larger than L2) or "groups"
+    (row groups: block-rows of similar length taken ``group_rows`` at a time
+    share each column's B panel and MMA; for skewed masks, STANDARD layout);
+    band_rows: block-rows per band item; group_rows: block-rows per row group
+    (2, 4 or 8; 0 = 4); ctas_per_sm: resident CTAs per SM of the
     row-split kernel (1..4), which share the SM's shared memory and TMEM so
     that one CTA's pipeline handoffs overlap another's MMAs.  Debugging knobs: wait_kcycles bounds every
     pipeline wait of the tcgen05 kernels (thousands of SM cycles; 0 = the
@@ -56,14 +59,17 @@ class KernelConfig:
     wait_kcycles: int = 0
     debug_hold_stage: int = 0
     ctas_per_sm: int = 0
+    group_rows: int = 0
 
     def __post_init__(self) -> None:
         if self.kernel not in ("auto", "simt", "tcgen05", "split_bf16"):
             raise ValueError(f"kernel must be 'auto', 'simt', 'tcgen05' or 'split_bf16', got {self.kernel!r}")
         if self.n_tile not in (0, 128, 256):
             raise ValueError(f"n_tile must be 0, 128 or 256, got {self.n_tile}")
-        if self.schedule not in ("auto", "rows", "bands"):
-            raise ValueError(f"schedule must be 'auto', 'rows' or 'bands', got {self.schedule!r}")
+        if self.schedule not in ("auto", "rows", "bands", "groups"):
+            raise ValueError(f"schedule must be 'auto', 'rows', 'bands' or 'groups', got {self.schedule!r}")
+        if self.group_rows not in (0, 2, 4, 8):
+            raise ValueError(f"group_rows must be 0, 2, 4 or 8, got {self.group_rows}")
         if self.debug_hold_stage not in (0, 1):
             raise ValueError("debug_hold_stage must be 0 or 1")
         if self.ctas_per_sm > 4:
@@ -83,7 +89,9 @@ class KernelConfig:
         c.row_cost = self.row_cost
         c.num_ctas = self.num_ctas
         c.group_blocks = self.group_blocks
-        c.schedule = {"auto": _lib.SCHEDULE_AUTO, "rows": _lib.SCHEDULE_ROWS, "bands": _lib.SCHEDULE_BANDS}[self.schedule]
+        # Row groups have their own entry point; its other knobs are these.
+        c.schedule = {"auto": _lib.SCHEDULE_AUTO, "rows": _lib.SCHEDULE_ROWS, "bands": _lib.SCHEDULE_BANDS,
+                      "groups": _lib.SCHEDULE_AUTO}[self.schedule]
         c.band_rows = self.band_rows
         c.wait_kcycles = self.wait_kcycles
         c.debug_hold_stage = self.debug_hold_stage
@@ -243,6 +251,97 @@ def _bsr_desc(a: BlockSparseMatrix) -> _lib.KairoBsr:
     return d
 
 
+class RowGroups:
+    """Row groups of a BSR matrix on its device (``kairo_bsr_stack_build``).
+
+    The block-rows, ordered by block count (longest first), are taken
+    ``rows_per_group`` at a time; each group's distinct column-blocks are its
+    stacked blocks.  Built once per matrix structure (it synchronises the
+    current stream once) and reused by every SpMM on that matrix.
+    """
+
+    def __init__(self, a: BlockSparseMatrix, rows_per_group: int) -> None:
+        lib = _lib.lib()
+        desc = _bsr_desc(a)
+        nbytes = ctypes.c_size_t(0)
+        with torch.cuda.device(a.device):
+            _lib.check(lib.kairo_bsr_stack_size(ctypes.byref(desc), rows_per_group, ctypes.byref(nbytes)),
+                       "kairo_bsr_stack_size")
+            self.mem = torch.empty(max(int(nbytes.value), 4), dtype=torch.uint8, device=a.device)
+            self.desc = _lib.KairoBsrStack()
+            _lib.check(lib.kairo_bsr_stack_build(ctypes.byref(desc), rows_per_group, self.mem.data_ptr(),
+                                                 self.mem.numel(), ctypes.byref(self.desc),
+                                                 _lib.stream_handle(a.device)), "kairo_bsr_stack_build")
+        self.rows_per_group = rows_per_group
+        self.ngroups = int(self.desc.ngroups)
+        self.nsuper = int(self.desc.nsuper)
+
+    def tables(self) -> dict[str, Tensor]:
+        """The group tables as int32 tensors viewing the group memory."""
+        d = self.desc
+        base = self.mem.data_ptr()
+        words = self.mem.view(torch.int32)
+
+        def view(ptr: int, count: int) -> Tensor:
+            off = (ptr - base) // 4
+            return words[off:off + count]
+
+        g, r, ns = self.ngroups, self.rows_per_group, self.nsuper
+        return {"row_map": view(d.row_map, g * r), "group_ptr": view(d.group_ptr, g + 1),
+                "super_col": view(d.super_col, ns), "super_mask": view(d.super_mask, ns),
+                "super_blk": view(d.super_blk, ns * r)}
+
+
+def bsr_row_groups(a: BlockSparseMatrix, rows_per_group: int = 4) -> RowGroups:
+    """The :class:`RowGroups` of ``a`` with ``rows_per_group`` rows (cached
+    on the matrix: its row_ptr / col_idx / blk_idx do not change)."""
+    cache = a.__dict__.get("_row_groups")
+    if cache is None:
+        cache = {}
+        object.__setattr__(a, "_row_groups", cache)
+    if rows_per_group not in cache:
+        cache[rows_per_group] = RowGroups(a, rows_per_group)
+    return cache[rows_per_group]
+
+
+# Automatic row groups: only for masks whose longest block-row is far above
+# the mean (a skewed mask), and only when grouping leaves at most this many
+# stacked blocks per block (each stacked block costs one B panel load).
+_GROUPS_MIN_SKEW = 8.0
+_GROUPS_MAX_RATIO = 0.6
+# Whether AUTO may take row groups at all (see the kernel notes: on the
+# measured skewed workload they do not yet beat the row-split schedule).
+_GROUPS_AUTO = False
+
+
+def _row_groups_for(a: BlockSparseMatrix, layout: int, config: KernelConfig | None) -> RowGroups | None:
+    cfg = config or KernelConfig()
+    rg = cfg.group_rows or 4
+    if cfg.schedule == "groups":
+        if layout != _lib.LAYOUT_STANDARD:
+            raise ValueError("the row-group schedule implements the STANDARD layout (block_sparse_mm_bsr) only")
+        return bsr_row_groups(a, rg)
+    if (not _GROUPS_AUTO or cfg.schedule != "auto" or cfg.kernel not in ("auto", "tcgen05")
+            or layout != _lib.LAYOUT_STANDARD):
+        return None
+    bm, bk = a.block_size
+    if (a.dtype not in (torch.float16, torch.bfloat16) or bm != bk or bm not in (16, 32) or a.nnzb == 0
+            or a.nbr > 16384 or a.nbc > 16384 or cfg.ctas_per_sm or cfg.num_ctas):
+        return None
+    mean = a.nnzb / max(a.nbr, 1)
+    if a.max_row_blocks < max(64.0, _GROUPS_MIN_SKEW * mean):
+        return None
+    choice = a.__dict__.get("_auto_groups", {})
+    if rg not in choice:
+        try:
+            groups = bsr_row_groups(a, rg)
+            choice[rg] = groups if groups.nsuper <= _GROUPS_MAX_RATIO * a.nnzb else None
+        except _lib.KairoError:
+            choice[rg] = None
+        object.__setattr__(a, "_auto_groups", choice)
+    return choice[rg]
+
+
 def describe(a: BlockSparseMatrix, n: int, *, linear: bool = False, config: KernelConfig | None = None) -> dict:
     """What ``block_sparse_mm_bsr`` (``linear=False``) or ``sparse_linear``
     (``linear=True``, N = rows of X) would run for ``a``: kernel, schedule,
@@ -252,15 +351,24 @@ def describe(a: BlockSparseMatrix, n: int, *, linear: bool = False, config: Kern
     desc = _bsr_desc(a)
     cfg = (config or KernelConfig()).to_c()
     layout = _lib.LAYOUT_LINEAR if linear else _lib.LAYOUT_STANDARD
+    groups = _row_groups_for(a, layout, config)
     with torch.cuda.device(a.device):
-        _lib.check(lib.kairo_bsr_spmm_describe(ctypes.byref(desc), layout, int(n), ctypes.byref(cfg),
-                                               ctypes.byref(plan)), "describe")
+        if groups is not None:
+            _lib.check(lib.kairo_bsr_spmm_stacked_describe(ctypes.byref(desc), ctypes.byref(groups.desc), int(n),
+                                                           ctypes.byref(cfg), ctypes.byref(plan)), "describe")
+        else:
+            _lib.check(lib.kairo_bsr_spmm_describe(ctypes.byref(desc), layout, int(n), ctypes.byref(cfg),
+                                                   ctypes.byref(plan)), "describe")
     kernel = {0: "none", _lib.KERNEL_SIMT: "simt", _lib.KERNEL_TCGEN05: "tcgen05",
               _lib.KERNEL_SPLIT_BF16: "split_bf16"}[plan.kernel]
-    schedule = {0: "none", _lib.SCHEDULE_ROWS: "rows", _lib.SCHEDULE_BANDS: "bands"}[plan.schedule]
-    return {"kernel": kernel, "schedule": schedule, "launches": plan.launches, "grid": plan.grid,
-            "n_tile": plan.n_tile, "stages": plan.stages, "group_blocks": plan.group_blocks, "rows": plan.rows,
-            "workspace_bytes": int(plan.workspace_bytes)}
+    schedule = {0: "none", _lib.SCHEDULE_ROWS: "rows", _lib.SCHEDULE_BANDS: "bands",
+                _lib.SCHEDULE_GROUPS: "groups"}[plan.schedule]
+    out = {"kernel": kernel, "schedule": schedule, "launches": plan.launches, "grid": plan.grid,
+           "n_tile": plan.n_tile, "stages": plan.stages, "group_blocks": plan.group_blocks, "rows": plan.rows,
+           "workspace_bytes": int(plan.workspace_bytes)}
+    if groups is not None:
+        out["stacked_blocks"] = groups.nsuper
+    return out
 
 
 def _launch(a: BlockSparseMatrix, b: Tensor, ldb: int, layout: int, n: int, out: Tensor, ldc: int,
@@ -269,16 +377,29 @@ def _launch(a: BlockSparseMatrix, b: Tensor, ldb: int, layout: int, n: int, out:
     desc = _bsr_desc(a)
     cfg = (config or KernelConfig()).to_c()
     dev = a.device
+    groups = _row_groups_for(a, layout, config)
+    if groups is not None and (config is None or config.schedule != "groups") and (ldb % 8 or b.data_ptr() % 16):
+        groups = None  # the row-group kernel copies B with TMA: 16-byte rows only
+    name = "kairo_bsr_spmm_stacked" if groups is not None else "kairo_bsr_spmm"
     with torch.cuda.device(dev):
         nbytes = ctypes.c_size_t(0)
-        _lib.check(lib.kairo_bsr_spmm_workspace_size(ctypes.byref(desc), layout, n, ctypes.byref(cfg),
-                                                     ctypes.byref(nbytes)), "kairo_bsr_spmm")
+        if groups is not None:
+            _lib.check(lib.kairo_bsr_spmm_stacked_workspace_size(ctypes.byref(desc), ctypes.byref(groups.desc), n,
+                                                                 ctypes.byref(cfg), ctypes.byref(nbytes)), name)
+        else:
+            _lib.check(lib.kairo_bsr_spmm_workspace_size(ctypes.byref(desc), layout, n, ctypes.byref(cfg),
+                                                         ctypes.byref(nbytes)), name)
         ws = _lib.workspace(nbytes.value, dev)
         if check_device:
-            _lib.take_pending_error(ws, "kairo_bsr_spmm")
-        _lib.check(lib.kairo_bsr_spmm(ctypes.byref(desc), b.data_ptr(), ldb, layout, n, out.data_ptr(), ldc,
-                                      _lib.kairo_dtype(out.dtype), ctypes.byref(cfg), ws.data_ptr(), ws.numel(),
-                                      _lib.stream_handle(dev)), "kairo_bsr_spmm")
+            _lib.take_pending_error(ws, name)
+        if groups is not None:
+            _lib.check(lib.kairo_bsr_spmm_stacked(ctypes.byref(desc), ctypes.byref(groups.desc), b.data_ptr(), ldb, n,
+                                                  out.data_ptr(), ldc, ctypes.byref(cfg), ws.data_ptr(), ws.numel(),
+                                                  _lib.stream_handle(dev)), name)
+        else:
+            _lib.check(lib.kairo_bsr_spmm(ctypes.byref(desc), b.data_ptr(), ldb, layout, n, out.data_ptr(), ldc,
+                                          _lib.kairo_dtype(out.dtype), ctypes.byref(cfg), ws.data_ptr(), ws.numel(),
+                                          _lib.stream_handle(dev)), name)
         if check_device:
             _lib.raise_on_device_error(ws)
 
