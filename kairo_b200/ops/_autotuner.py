@@ -10,7 +10,8 @@ On B200 the search space gains the Blackwell launch knobs of the tcgen05
 kernel (``BLACKWELL_VARIANTS``): ``n_tile`` (128 or 256 columns of C per work
 item, i.e. one or two M=128 MMAs sharing each block), ``stages``
 (shared-memory pipeline depth), ``row_cost`` (scheduler weight of a
-block-row), ``schedule`` (row split or bands), ``group_blocks`` (blocks
+block-row), ``schedule`` (row split, bands or row groups of
+``GROUP_VARIANTS`` rows), ``group_blocks`` (blocks
 per pipeline stage) and ``ctas_per_sm`` (resident CTAs per SM).  They are returned as extra keys.  Candidate tiles are
 built as tile_m x tile_k blocks (the reference times square tile_m tiles
 whatever tile_k is), so each candidate is timed with the kernel it would
@@ -94,6 +95,10 @@ BLACKWELL_VARIANTS: tuple[tuple[int, int, int, str, int, int], ...] = (
     (0, 0, 0, "rows", 8, 1),
     (256, 4, 0, "rows", 0, 1),
 )
+
+# Row-group sizes also timed by ``time_kernel_configs`` (schedule "groups";
+# a matrix the row groups do not support times as inf).
+GROUP_VARIANTS: tuple[int, ...] = (2, 4)
 
 BENCH_WARMUP = 2
 BENCH_ITERS = 5
@@ -218,6 +223,7 @@ class TileAutotuner:
             candidates = [KernelConfig(n_tile=nt, stages=st, row_cost=rc, schedule=sc, group_blocks=gb,
                                        ctas_per_sm=per_sm)
                           for nt, st, rc, sc, gb, per_sm in BLACKWELL_VARIANTS]
+            candidates += [KernelConfig(schedule="groups", group_rows=rg) for rg in GROUP_VARIANTS]
         if B is None:
             B = torch.randn(a.shape[1], N, device=a.device).to(a.dtype)
         out = torch.empty(a.shape[0], N, dtype=torch.float32, device=a.device)
@@ -247,7 +253,7 @@ class TileAutotuner:
         self._cache[key] = {"kernel": best.kernel, "n_tile": best.n_tile, "stages": best.stages,
                             "row_cost": best.row_cost, "num_ctas": best.num_ctas, "schedule": best.schedule,
                             "group_blocks": best.group_blocks, "band_rows": best.band_rows,
-                            "ctas_per_sm": best.ctas_per_sm}
+                            "ctas_per_sm": best.ctas_per_sm, "group_rows": best.group_rows}
         return best
 
     def clear_cache(self) -> None:
