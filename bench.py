@@ -226,6 +226,8 @@ def workload_spec(args):
     if args.shape:
         m, k, n = (int(x) for x in args.shape.lower().split("x"))
         spec = spec.scaled(m, k, n)
+    if args.sparsity is not None:
+        spec = dataclasses.replace(spec, name=f"{spec.name}@sparsity{args.sparsity}", sparsity=args.sparsity)
     return spec
 
 
@@ -1075,6 +1077,7 @@ def main() -> None:
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--shape", default="", help="MxKxN override of the workload's sizes (same density), "
                     "for profiling smaller cases")
+    ap.add_argument("--sparsity", type=float, default=None, help="block sparsity override of the workload")
     ap.add_argument("--kernel", choices=("auto", "simt", "tcgen05", "split_bf16"), default="auto",
                     help="kernel family (split_bf16: fp32 workloads on the tensor cores, opt-in)")
     ap.add_argument("--n-tile", type=int, default=0)

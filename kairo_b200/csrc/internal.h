@@ -87,6 +87,7 @@ struct TcPlan {
   int hold_stage;          // kairo_spmm_config.debug_hold_stage
   int ctas_per_sm;         // resident CTAs per SM the shared-memory budget was split for
   int rg;                  // block-rows per item (1, or the row-group size)
+  int packed;              // stages hold their panels, then their blocks packed (rg = 1, 16-row blocks)
 };
 
 // TMA tensor maps (tma_maps.cu).  make_operand_maps builds the block-storage

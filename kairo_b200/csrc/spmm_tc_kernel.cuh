@@ -84,7 +84,8 @@ struct TcArgs {
   // count groups / stacked blocks, and these two tables complete them.
   const int32_t* stack_blk;  // [nnzb][RG]: stored-block index of each present block
   const int32_t* row_map;    // [nbr][RG]: block-row of each group slot, -1 past the last
-  int32_t a_batch;           // RG = 1: tmap_a_run copies a whole stage of consecutive blocks
+  int32_t packed;            // RG = 1: a stage holds its B panels, then its blocks packed
+  int32_t a_batch;           // packed: tmap_a_run copies a whole stage of consecutive blocks
 };
 
 struct RowItem {
@@ -228,10 +229,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int S = args.stages;
   const int GB = args.group;
-  // A stage holds GB blocks.  RG = 1: their B panels, then the blocks
-  // packed (so that consecutive stored blocks arrive with one copy); RG > 1:
-  // GB slots of one panel and RG blocks.
-  const uint32_t STAGE_BYTES = static_cast<uint32_t>(tc_stage_bytes(BM, BK, NT, RG, GB));
+  // A stage holds GB blocks: GB slots of a B panel and its block (RG > 1:
+  // RG blocks), each slot padded to 1 KiB, or, packed (RG = 1), the GB
+  // panels and then the GB blocks side by side, so that consecutive stored
+  // blocks arrive with one copy.
+  const bool packed = RG == 1 && args.packed;
+  const uint32_t STAGE_BYTES = static_cast<uint32_t>(tc_stage_bytes(BM, BK, NT, RG, GB, packed));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * STAGE_BYTES);
   uint64_t* empty = full + S;
   uint64_t* tfull = empty + S;
@@ -263,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 0 && lane == 0) {
     ptx::prefetch_tmap(&tmap_a);
-    if (RG == 1 && args.a_batch) ptx::prefetch_tmap(&tmap_a_run);
+    if (packed && args.a_batch) ptx::prefetch_tmap(&tmap_a_run);
     ptx::prefetch_tmap(&tmap_b);
   }
   if (warp == 1) {
@@ -357,20 +360,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t mine = (lane >= j0 && lane < j0 + take) ? 1u : 0u;
           uint8_t* stage = smem + gidx * STAGE_BYTES;
           const int js = gpos + (lane - j0);  // this lane's block slot in the stage
-          uint8_t* st = RG == 1 ? stage + js * PANEL_BYTES : stage + js * SLOT_BYTES;  // its B panel
+          uint8_t* st = packed ? stage + js * PANEL_BYTES : stage + js * SLOT_BYTES;  // its B panel
           if constexpr (RG == 1) {
             ptx::mbar_expect_tx_if(mine, &full[gidx], TX_BYTES);
             // A whole stage of consecutive stored blocks (a long block-row
             // with identity block order) arrives with one copy of GB * BM
             // rows; otherwise each lane copies its block.
             const int mb0 = __shfl_sync(0xffffffffu, mb, j0);
-            const bool run = args.a_batch && gpos == 0 && take == GB &&
+            const bool run = packed && args.a_batch && gpos == 0 && take == GB &&
                              __all_sync(0xffffffffu, !mine || mb == mb0 + (lane - j0));
             uint8_t* blocks = stage + GB * PANEL_BYTES;
             if (run) {
               ptx::tma_load_2d_if(lane == j0 ? 1u : 0u, blocks, &tmap_a_run, 0, mb0 * BM, &full[gidx], pol_a);
             } else {
-              ptx::tma_load_2d_if(mine, blocks + js * A_BYTES, &tmap_a, 0, mb * BM, &full[gidx], pol_a);
+              ptx::tma_load_2d_if(mine, packed ? blocks + js * A_BYTES : st + PANEL_BYTES, &tmap_a, 0, mb * BM,
+                                  &full[gidx], pol_a);
             }
           } else {
             // The panel plus the group's present blocks, block of slot r at
@@ -444,8 +448,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t b_lo0 = static_cast<uint32_t>(bdesc0), b_hi = static_cast<uint32_t>(bdesc0 >> 32);
     constexpr uint32_t SLOT16 = SLOT_BYTES >> 4;
     constexpr uint32_t PANEL16 = PANEL_BYTES >> 4;
-    constexpr uint32_t PAN_STEP16 = RG == 1 ? PANEL16 : SLOT16;
-    constexpr uint32_t BLK_STEP16 = RG == 1 ? static_cast<uint32_t>(A_BYTES >> 4) : SLOT16;
+    const uint32_t PAN_STEP16 = packed ? PANEL16 : SLOT16;
+    const uint32_t BLK_STEP16 = packed ? static_cast<uint32_t>(A_BYTES >> 4) : SLOT16;
     uint32_t pan16 = 0;  // (byte offset of the current block's B panel) >> 4
     uint32_t blk16 = 0;  // (byte offset of the current block) >> 4
     walk_items(args, s_range, e_range, i_start, lane, [&](const RowItem& it) -> bool {
@@ -464,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = __shfl_sync(0xffffffffu, ok, 0);
           if (!ok) return false;
           pan16 = (static_cast<uint32_t>(midx) * STAGE_BYTES) >> 4;
-          blk16 = pan16 + (RG == 1 ? static_cast<uint32_t>(GB) * PANEL16 : PANEL16);
+          blk16 = pan16 + (packed ? static_cast<uint32_t>(GB) * PANEL16 : PANEL16);
         }
         // Blocks [p, p + seg) all live in the current stage group.
         const int seg = min(it.p1 - p, GB - mpos);

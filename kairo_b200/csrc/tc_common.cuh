@@ -40,11 +40,12 @@ constexpr int stage_bytes(int bm, int bk, int nt, int rg = 1) {
 }
 
 // Bytes of one stage of `group` blocks of the row-split tcgen05 kernel:
-// rg = 1: the group's B panels, then its blocks packed, rounded up to 1 KiB;
-// rg > 1: `group` slots of one panel and rg blocks (stage_bytes each).
-__host__ __device__ constexpr int tc_stage_bytes(int bm, int bk, int nt, int rg, int group) {
-  return rg == 1 ? (group * (nt * 128 * bk * 2 + bm * bk * 2) + 1023) / 1024 * 1024
-                 : group * (nt * 128 * bk * 2 + (rg * bm * bk * 2 + 1023) / 1024 * 1024);
+// `group` slots of one B panel and rg blocks (stage_bytes each), or, packed
+// (rg = 1), the group's panels and then its blocks side by side, rounded up
+// to 1 KiB.
+__host__ __device__ constexpr int tc_stage_bytes(int bm, int bk, int nt, int rg, int group, bool packed) {
+  return packed ? (group * (nt * 128 * bk * 2 + bm * bk * 2) + 1023) / 1024 * 1024
+                : group * (nt * 128 * bk * 2 + (rg * bm * bk * 2 + 1023) / 1024 * 1024);
 }
 
 template <typename TOut>

@@ -12,7 +12,7 @@ import torch
 from oracle import oracle
 from kairo_b200 import _lib
 from kairo_b200.ops import KernelConfig, TileAutotuner, block_sparse_mm_bsr, bsr_from_tiles, describe
-from kairo_b200.ops._autotuner import BLACKWELL_VARIANTS, CANDIDATE_CONFIGS
+from kairo_b200.ops._autotuner import BLACKWELL_VARIANTS, CANDIDATE_CONFIGS, GROUP_VARIANTS
 from kairo_b200.workloads import WorkloadSpec, generate
 from tests.conftest import rel_fro
 
@@ -57,7 +57,8 @@ def test_best_kernel_config_on_a_matrix():
     a = bsr_from_tiles(p.tiles.cuda(), p.row_ids.cuda(), p.col_ids.cuda(), (spec.m, spec.k))
     tuner = TileAutotuner()
     timed = tuner.time_kernel_configs(a, spec.n)
-    assert len(timed) == len(BLACKWELL_VARIANTS)
+    assert len(timed) == len(BLACKWELL_VARIANTS) + len(GROUP_VARIANTS)
+    assert sum(kc.schedule == "groups" for kc, _ in timed) == len(GROUP_VARIANTS)
     for kc, t in timed:
         # a variant whose pipeline does not fit this block shape (e.g. 8
         # blocks of 256 columns per stage) is skipped as inf, as in the
