@@ -218,9 +218,12 @@ kairo_status tc_launch(const kairo_bsr* a, const void* b, int64_t ldb, int32_t l
   CUtensorMap map_run = map_a;
   int a_batch = 0;
   if (plan.packed && plan.group > 1 && plan.group * plan.bm <= 256) {
-    st = make_block_run_map(a, plan.group, &map_run);
-    if (st) return st;
-    a_batch = 1;
+    // Optional: without this map every block is copied on its own.
+    if (make_block_run_map(a, plan.group, &map_run) == KAIRO_STATUS_SUCCESS) {
+      a_batch = 1;
+    } else {
+      map_run = map_a;
+    }
   }
 
   TcArgs args{};
