@@ -247,3 +247,36 @@ def test_autotuner_candidates_and_key():
     # the reference's 4-argument key is unchanged; dtype and block are appended
     assert _cache_key(256, 256, 128, 0.5) == "512_512_128_0.5"
     assert _cache_key(256, 256, 128, 0.5, _t.bfloat16, 32) == "512_512_128_0.5_bfloat16_b32"
+
+
+def test_row_group_knobs_and_choice_without_a_device(monkeypatch):
+    """Row groups: the knobs are validated, the stack descriptor has the C
+    layout, and the schedule choice is made on the host (AUTO leaves them
+    off unless switched on; a non-skewed matrix never builds them; the
+    LINEAR layout refuses an explicit request)."""
+    import ctypes
+
+    from kairo_b200 import _lib
+    from kairo_b200.ops import KernelConfig
+    from kairo_b200.ops import spmm as spmm_mod
+
+    for r in (0, 2, 4, 8):
+        assert KernelConfig(schedule="groups", group_rows=r).to_c().schedule == _lib.SCHEDULE_AUTO
+    for bad in (1, 3, 16):
+        with pytest.raises(ValueError):
+            KernelConfig(group_rows=bad)
+    assert ctypes.sizeof(_lib.KairoBsrStack) == 56
+
+    nbr, bs = 64, 16
+    counts = torch.full((nbr,), 3, dtype=torch.int32)
+    row_ptr = torch.cat([torch.zeros(1, dtype=torch.int32), torch.cumsum(counts, 0).to(torch.int32)])
+    nnzb = int(row_ptr[-1])
+    a = BlockSparseMatrix(row_ptr=row_ptr, col_idx=torch.arange(nnzb, dtype=torch.int32) % nbr,
+                          blocks=torch.zeros(nnzb, bs, bs, dtype=torch.float16), shape=(nbr * bs, nbr * bs),
+                          block_size=(bs, bs), max_row_blocks=3)
+    assert spmm_mod._row_groups_for(a, _lib.LAYOUT_STANDARD, None) is None
+    monkeypatch.setattr(spmm_mod, "_GROUPS_AUTO", True)
+    assert spmm_mod._row_groups_for(a, _lib.LAYOUT_STANDARD, None) is None  # rows of equal length
+    assert spmm_mod._row_groups_for(a, _lib.LAYOUT_STANDARD, KernelConfig(schedule="rows")) is None
+    with pytest.raises(ValueError):
+        spmm_mod._row_groups_for(a, _lib.LAYOUT_LINEAR, KernelConfig(schedule="groups"))
