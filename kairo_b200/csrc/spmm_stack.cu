@@ -483,6 +483,7 @@ kairo_status kairo_bsr_spmm_stacked(const kairo_bsr* a, const kairo_bsr_stack* s
   args.vec_store = 0;
   args.stack_blk = s->super_blk;
   args.row_map = s->row_map;
+  args.c_vec4 = ((reinterpret_cast<uintptr_t>(c) & 15u) == 0) && (ldc % 4 == 0) ? 1 : 0;
   args.packed = 0;
   args.a_batch = 0;
   cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(fn), cudaFuncAttributeMaxDynamicSharedMemorySize,

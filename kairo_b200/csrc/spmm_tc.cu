@@ -257,6 +257,7 @@ kairo_status tc_launch(const kairo_bsr* a, const void* b, int64_t ldb, int32_t l
   args.hold_stage = plan.hold_stage;
   args.wait_cycles = plan.wait_cycles;
   args.vec_store = linear && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0) && ((ldc * osz) % 16 == 0) ? 1 : 0;
+  args.c_vec4 = !linear && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0) && (ldc % 4 == 0) ? 1 : 0;
   args.packed = plan.packed;
   args.a_batch = a_batch;
 

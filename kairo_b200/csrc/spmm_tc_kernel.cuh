@@ -86,7 +86,30 @@ struct TcArgs {
   const int32_t* row_map;    // [nbr][RG]: block-row of each group slot, -1 past the last
   int32_t packed;            // RG = 1: a stage holds its B panels, then its blocks packed
   int32_t a_batch;           // packed: tmap_a_run copies a whole stage of consecutive blocks
+  int32_t c_vec4;            // STANDARD: C rows may be written with 16-byte stores
 };
+
+// Writes zeros to rows i*BM .. i*BM+BM-1 and columns n0 .. n0+NT*128-1 of
+// the row-major fp32 C (clamped to M x N), for a block-row without blocks:
+// the 128 epilogue threads (t = 0..127) store 16-byte vectors, a warp 512
+// contiguous bytes of one row.
+template <int BM, int NT>
+__device__ __forceinline__ void zero_c_rows(const TcArgs& a, int i, int n0, int t) {
+  float* c = static_cast<float*>(a.c);
+  constexpr int V = NT * 32;  // 16-byte vectors per row of the item
+#pragma unroll
+  for (int q = t; q < BM * V; q += 128) {
+    const int r = i * BM + q / V;
+    const int col = n0 + (q % V) * 4;
+    if (r >= a.m || col >= a.n) continue;
+    float* dst = c + static_cast<int64_t>(r) * a.ldc + col;
+    if (a.c_vec4 && col + 4 <= a.n) {
+      __stcs(reinterpret_cast<float4*>(dst), make_float4(0.f, 0.f, 0.f, 0.f));
+    } else {
+      for (int u = 0; u < 4 && col + u < a.n; ++u) __stcs(dst + u, 0.f);
+    }
+  }
+}
 
 struct RowItem {
   int chunk;       // global chunk index
@@ -550,16 +573,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // next item, and stored (or written to the partial tile).
         const int32_t* rmap = args.row_map + static_cast<int64_t>(it.row) * RG;
         if (it.kind == kZero) {
-          float z[16];
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) z[jj] = 0.f;
           for (int r = 0; r < RG; ++r) {
             const int orow = __ldg(rmap + r);
-            if (orow < 0) continue;
-#pragma unroll
-            for (int t = 0; t < NT; ++t)
-#pragma unroll
-              for (int j0 = 0; j0 < BM; j0 += 16) store16<false, TOut>(args, orow, BM, j0, n0 + t * 128 + e, z);
+            if (orow >= 0) zero_c_rows<BM, NT>(args, orow, n0, threadIdx.x - 64);
           }
           return true;
         }
@@ -636,13 +652,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       }
       if (it.kind == kZero) {
-        float z[16];
+        if constexpr (!LINEAR) {
+          zero_c_rows<BM, NT>(args, it.row, n0, threadIdx.x - 64);
+        } else {
+          float z[16];
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) z[jj] = 0.f;
+          for (int jj = 0; jj < 16; ++jj) z[jj] = 0.f;
 #pragma unroll
-        for (int t = 0; t < NT; ++t)
+          for (int t = 0; t < NT; ++t)
 #pragma unroll
-          for (int j0 = 0; j0 < BM; j0 += 16) store16<LINEAR, TOut>(args, it.row, BM, j0, n0 + t * 128 + e, z);
+            for (int j0 = 0; j0 < BM; j0 += 16) store16<LINEAR, TOut>(args, it.row, BM, j0, n0 + t * 128 + e, z);
+        }
         return true;
       }
       int ok = ptx::wait_parity(&tfull[slot], aphase, abort_flag, args.err, kTagTmemFull, args.wait_cycles, 200);
