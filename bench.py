@@ -759,7 +759,8 @@ def run_backward(args) -> None:
 
 def run_tune(args) -> None:
     """The autotuner's candidates on a named workload: every launch variant
-    of BLACKWELL_VARIANTS (plus the library default) timed on the actual
+    of BLACKWELL_VARIANTS and GROUP_VARIANTS (the first is the library
+    default) timed on the actual
     matrix by TileAutotuner.time_kernel_configs (CUDA events, median of
     BENCH_ITERS, L2 not flushed between calls), and the one
     best_kernel_config picks.  Evidence for the library's defaults."""
@@ -782,7 +783,8 @@ def run_tune(args) -> None:
         except Exception as exc:  # noqa: BLE001 - a variant this shape does not support
             plan = {"unsupported": str(exc)}
         rows.append({"n_tile": kc.n_tile, "stages": kc.stages, "row_cost": kc.row_cost, "schedule": kc.schedule,
-                     "group_blocks": kc.group_blocks, "ctas_per_sm": kc.ctas_per_sm, "ms": ms,
+                     "group_blocks": kc.group_blocks, "ctas_per_sm": kc.ctas_per_sm, "group_rows": kc.group_rows,
+                     "ms": ms,
                      "tflops": flops(spec) / (ms / 1e3) / 1e12,
                      "plan": plan})
     best = tuner.best_kernel_config(a, spec.n)
