@@ -14,10 +14,14 @@
 //   operand B = the nonzero block, K-major (row-major block storage);
 //   D in TMEM = 128 lanes (columns of C) x bm fp32 columns (rows of C).
 //
-// Roles (192 threads, one CTA per SM, persistent):
-//   warp 0      TMA producer: one A block + the matching B panel per stage;
+// Roles (192 threads; one or more persistent CTAs per SM, each with its own
+// share of shared memory and TMEM):
+//   warp 0      TMA producer: a stage holds `group` blocks and their B panels,
+//               one lane per block; packed stages (16-row blocks) copy a run
+//               of consecutive stored blocks with one TMA copy;
 //   warp 1      TMEM allocator and single-thread MMA issuer;
-//   warps 2..5  epilogue: TMEM -> registers -> C, or -> a partial slot.
+//   warps 2..5  epilogue: TMEM -> registers -> C, or -> a partial slot; a
+//               block-row without blocks is zeroed with 16-byte stores.
 // Smem stages are released by tcgen05.commit; two TMEM accumulator slots let
 // the epilogue of one block-row overlap the MMAs of the next.
 //
