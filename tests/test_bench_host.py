@@ -81,3 +81,17 @@ def test_block_row_errors_localise_one_bad_row():
     assert float(rows[30]) == 0.0
     # the whole-matrix error of the same difference is far below the bar
     assert rel_fro_chunked(c, ref, chunk_rows=700) < 1e-3 < float(rows.max())
+
+
+def test_workload_overrides_shape_and_sparsity():
+    """--shape and --sparsity derive a named variant of a workload (its own
+    name, so a committed traffic capture of the original never applies)."""
+    import argparse
+
+    args = argparse.Namespace(workload="fp16_zipf", shape="", sparsity=None)
+    assert bench.workload_spec(args) == WORKLOADS["fp16_zipf"]
+    args = argparse.Namespace(workload="fp16_zipf", shape="8192x8192x128", sparsity=0.999)
+    spec = bench.workload_spec(args)
+    assert (spec.m, spec.k, spec.n, spec.sparsity, spec.mask) == (8192, 8192, 128, 0.999, "zipf")
+    assert spec.name != WORKLOADS["fp16_zipf"].name and "sparsity0.999" in spec.name
+    assert spec.nnzb == max(1, int(spec.nbr * spec.nbc * (1 - 0.999)))
