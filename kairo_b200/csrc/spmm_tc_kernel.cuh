@@ -240,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int PANEL_BYTES = NT * 128 * BK * 2;
   constexpr int A_BYTES = BM * BK * 2;
   constexpr int A_BYTES_PAD = (RG * A_BYTES + 1023) / 1024 * 1024;
-  constexpr int SLOT_BYTES = PANEL_BYTES + A_BYTES_PAD;  // RG > 1: a B panel + RG blocks
+  constexpr int SLOT_BYTES = PANEL_BYTES + A_BYTES_PAD;  // a B panel and its block (RG blocks), unpacked stages
   constexpr uint32_t TX_BYTES = PANEL_BYTES + A_BYTES;
   constexpr int BME = BM * RG;        // accumulator columns of one 128-column sub-tile
   constexpr int ACC_COLS = NT * BME;  // one accumulator: NT sub-tiles of BME fp32 columns
